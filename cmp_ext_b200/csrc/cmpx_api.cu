@@ -1,0 +1,436 @@
+// C-ABI entry points of libcmpx.so: argument checks, path selection, TMA
+// descriptor construction, workspace management, and the reference-compatible
+// launch_matmul_* / launch_add_bias_* symbols.
+//
+// Reference boundary being replaced: the C++ launchers declared at
+// src/main.cpp:12-19 and defined in src/cuda/{fp16,fp32,bf16}_matmul.cu.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "internal.h"
+
+namespace cmpx {
+
+__device__ int g_device_error = 0;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct DeviceState {
+  bool init = false;
+  int status = CMPX_OK;
+  DeviceInfo info{};
+  int* err_word = nullptr;
+  std::mutex ws_mu;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+
+DeviceState g_dev[kMaxDevices];
+std::mutex g_init_mu;
+EncodeTiledFn g_encode = nullptr;
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? CMPX_OK : CMPX_ERR_CUDA; }
+
+// Resolves (once) the per-device facts and the driver's tensor-map encoder.
+int device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CMPX_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return CMPX_ERR_UNSUPPORTED;
+  DeviceState& d = g_dev[dev];
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (!d.init) {
+    d.init = true;
+    d.status = CMPX_OK;
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.info.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.info.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+            cudaSuccess) {
+      d.status = CMPX_ERR_CUDA;
+    } else if (major != 10 || minor != 0) {
+      d.status = CMPX_ERR_UNSUPPORTED;  // kernels are built for sm_100a only
+    } else if (cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err_word), g_device_error) != cudaSuccess) {
+      d.status = CMPX_ERR_CUDA;
+    }
+    if (d.status == CMPX_OK && g_encode == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr) {
+        d.status = CMPX_ERR_CUDA;
+      } else {
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+      }
+    }
+  }
+  *out = &d;
+  return d.status;
+}
+
+// Grow-only library-managed workspace, zero-filled when (re)allocated.  It is
+// shared by every call on the device: concurrent calls on different streams
+// that need scratch must pass their own workspace.
+int library_workspace(DeviceState& d, size_t bytes, void** out) {
+  std::lock_guard<std::mutex> lk(d.ws_mu);
+  if (d.ws_bytes < bytes) {
+    if (d.ws != nullptr) {
+      cudaDeviceSynchronize();  // earlier launches may still read the old buffer
+      cudaFree(d.ws);
+      d.ws = nullptr;
+      d.ws_bytes = 0;
+    }
+    size_t want = bytes + bytes / 4;
+    if (cudaMalloc(&d.ws, want) != cudaSuccess) {
+      cudaGetLastError();
+      return CMPX_ERR_NO_MEMORY;
+    }
+    if (cudaMemset(d.ws, 0, want) != cudaSuccess) return CMPX_ERR_CUDA;
+    d.ws_bytes = want;
+  }
+  *out = d.ws;
+  return CMPX_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 3-D tiled map {inner, rows, batch}, 128-byte swizzle.
+int encode_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
+              uint64_t ld, uint64_t bstride, uint32_t box_inner, uint32_t box_rows) {
+  const uint64_t E = uint64_t(elem_bytes(dtype));
+  if (batch <= 1 || bstride == 0) bstride = rows * ld;
+  if (batch < 1) batch = 1;
+  const CUtensorMapDataType dt = dtype == CMPX_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : dtype == CMPX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t dims[3] = {inner, rows, batch};
+  cuuint64_t strides[2] = {ld * E, bstride * E};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CMPX_OK : CMPX_ERR_CUDA;
+}
+
+int env_forced_path() {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* e = std::getenv("CMPX_FORCE_PATH");
+    forced = CMPX_PATH_AUTO;
+    if (e != nullptr) {
+      if (!std::strcmp(e, "tc")) forced = CMPX_PATH_TC;
+      else if (!std::strcmp(e, "skinny")) forced = CMPX_PATH_SKINNY;
+      else if (!std::strcmp(e, "simt")) forced = CMPX_PATH_SIMT;
+    }
+  }
+  return forced;
+}
+
+int validate(const cmpx_gemm_args* a) {
+  if (a == nullptr) return CMPX_ERR_INVALID_ARG;
+  if (a->dtype != CMPX_F16 && a->dtype != CMPX_BF16 && a->dtype != CMPX_F32) return CMPX_ERR_INVALID_ARG;
+  if (a->b_layout != CMPX_B_KN && a->b_layout != CMPX_B_NK) return CMPX_ERR_INVALID_ARG;
+  if (a->path < CMPX_PATH_AUTO || a->path > CMPX_PATH_SIMT) return CMPX_ERR_INVALID_ARG;
+  if (a->batch < 0 || a->M < 0 || a->N < 0 || a->K < 0) return CMPX_ERR_INVALID_ARG;
+  const int64_t lim = (int64_t(1) << 31) - 1;
+  if (a->M > lim || a->N > lim || a->K > lim || a->batch > 65535) return CMPX_ERR_UNSUPPORTED;
+  if (a->batch == 0 || a->M == 0 || a->N == 0) return CMPX_OK;
+  if (a->C == nullptr) return CMPX_ERR_INVALID_ARG;
+  if (a->ldc < a->N) return CMPX_ERR_INVALID_ARG;
+  if (a->K > 0) {
+    if (a->A == nullptr || a->B == nullptr) return CMPX_ERR_INVALID_ARG;
+    if (a->lda < a->K) return CMPX_ERR_INVALID_ARG;
+    if (a->ldb < (a->b_layout == CMPX_B_KN ? a->N : a->K)) return CMPX_ERR_INVALID_ARG;
+  }
+  if (a->stride_a < 0 || a->stride_b < 0 || a->stride_c < 0) return CMPX_ERR_INVALID_ARG;
+  return CMPX_OK;
+}
+
+Gemm to_gemm(const cmpx_gemm_args* a) {
+  Gemm g;
+  g.dtype = a->dtype;
+  g.A = a->A;
+  g.B = a->B;
+  g.C = a->C;
+  g.bias = a->bias;
+  g.batch = a->batch;
+  g.M = a->M;
+  g.N = a->N;
+  g.K = a->K;
+  g.lda = a->lda;
+  g.ldb = a->ldb;
+  g.ldc = a->ldc;
+  g.sa = a->batch > 1 ? a->stride_a : a->M * a->lda;
+  g.sb = a->batch > 1 ? a->stride_b : (a->b_layout == CMPX_B_KN ? a->K * a->ldb : a->N * a->ldb);
+  g.sc = a->batch > 1 ? a->stride_c : a->M * a->ldc;
+  g.b_kmajor = a->b_layout == CMPX_B_NK ? 1 : 0;
+  return g;
+}
+
+// Can the TMA engine describe A and B as given (fp16/bf16) and can the
+// epilogue use 16-byte stores on C?
+bool tma_ok_16bit(const Gemm& g) {
+  const int64_t E = 2;
+  auto ok = [&](const void* p, int64_t ld, int64_t bs) {
+    return aligned16(p) && (ld * E) % 16 == 0 && (g.batch <= 1 || (bs * E) % 16 == 0);
+  };
+  return ok(g.A, g.lda, g.sa) && ok(g.B, g.ldb, g.sb) && ok(g.C, g.ldc, g.sc);
+}
+
+// fp32 3xTF32: operands are re-packed by the split pre-pass, so only the
+// packed row lengths (K for A; N or K for B) and C need 16-byte alignment.
+bool tma_ok_f32(const Gemm& g) {
+  const bool a_ok = (g.K * 4) % 16 == 0;
+  const bool b_ok = g.b_kmajor ? (g.K * 4) % 16 == 0 : (g.N * 4) % 16 == 0;
+  const bool c_ok = aligned16(g.C) && (g.ldc * 4) % 16 == 0 && (g.batch <= 1 || (g.sc * 4) % 16 == 0);
+  return a_ok && b_ok && c_ok;
+}
+
+int choose_path(const Gemm& g, int requested) {
+  int forced = requested != CMPX_PATH_AUTO ? requested : env_forced_path();
+  if (g.K == 0) return CMPX_PATH_SIMT;  // fill kernel
+  if (g.dtype == CMPX_F32) {
+    const bool ok = tma_ok_f32(g);
+    if (forced == CMPX_PATH_SKINNY) return -1;
+    if (forced == CMPX_PATH_TC) return ok ? CMPX_PATH_TC : -1;
+    if (forced == CMPX_PATH_SIMT) return CMPX_PATH_SIMT;
+    const double work = double(g.batch) * double(g.M) * double(g.N) * double(g.K);
+    return (ok && work >= double(1 << 22)) ? CMPX_PATH_TC : CMPX_PATH_SIMT;
+  }
+  const bool ok = tma_ok_16bit(g);
+  if (forced == CMPX_PATH_TC) return ok ? CMPX_PATH_TC : -1;
+  if (forced == CMPX_PATH_SKINNY) return (ok && g.M <= 64) ? CMPX_PATH_SKINNY : -1;
+  if (forced == CMPX_PATH_SIMT) return CMPX_PATH_SIMT;
+  if (!ok) return CMPX_PATH_SIMT;
+  return g.M <= 64 ? CMPX_PATH_SKINNY : CMPX_PATH_TC;
+}
+
+size_t f32_split_bytes(const Gemm& g) {
+  const size_t a = size_t(g.batch) * size_t(g.M) * size_t(g.K);
+  const size_t b = size_t(g.batch) * size_t(g.K) * size_t(g.N);
+  auto up = [](size_t x) { return (x * 4 + 255) / 256 * 256; };
+  return 2 * up(a) + 2 * up(b);
+}
+
+size_t workspace_for(const Gemm& g, int path, const DeviceInfo& dev) {
+  if (path == CMPX_PATH_SKINNY) return skinny_workspace_bytes(g, dev);
+  if (path == CMPX_PATH_TC && g.dtype == CMPX_F32) return f32_split_bytes(g);
+  return 0;
+}
+
+int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
+  int st = validate(args);
+  if (st != CMPX_OK) return st;
+  if (args->batch == 0 || args->M == 0 || args->N == 0) return CMPX_OK;
+  DeviceState* d = nullptr;
+  st = device_state(&d);
+  if (st != CMPX_OK) return st;
+  const Gemm g = to_gemm(args);
+  const int path = choose_path(g, args->path);
+  if (path < 0) return CMPX_ERR_UNSUPPORTED;
+  if (g.K == 0) return cuda_status(launch_fill_bias(g, s));
+  if (path == CMPX_PATH_SIMT) return cuda_status(launch_simt(g, s));
+
+  void* ws = nullptr;
+  const size_t need = workspace_for(g, path, d->info);
+  if (need > 0) {
+    if (args->workspace != nullptr) {
+      if (args->workspace_bytes < need) return CMPX_ERR_WORKSPACE;
+      if (!aligned16(args->workspace)) return CMPX_ERR_INVALID_ARG;
+      ws = args->workspace;
+    } else {
+      st = library_workspace(*d, need, &ws);
+      if (st != CMPX_OK) return st;
+    }
+  }
+
+  if (path == CMPX_PATH_SKINNY) {
+    const uint32_t mn = uint32_t(skinny_mn(g.M));
+    CUtensorMap tB, tA;
+    st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 128)
+                    : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
+    if (st != CMPX_OK) return st;
+    st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.batch, g.lda, g.sa, 64, mn);
+    if (st != CMPX_OK) return st;
+    return cuda_status(launch_skinny(g, tB, tA, ws, d->info, d->err_word, s));
+  }
+
+  if (g.dtype != CMPX_F32) {
+    CUtensorMap tA, tB;
+    st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.batch, g.lda, g.sa, 64, 128);
+    if (st != CMPX_OK) return st;
+    st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 256)
+                    : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
+    if (st != CMPX_OK) return st;
+    return cuda_status(launch_tc_f16(g, tA, tB, 256, d->info, d->err_word, s));
+  }
+
+  // fp32: split A and B into packed tf32 hi/lo, then 3xTF32 on the tensor cores.
+  const size_t a_elems = size_t(g.batch) * size_t(g.M) * size_t(g.K);
+  const size_t b_elems = size_t(g.batch) * size_t(g.K) * size_t(g.N);
+  auto up = [](size_t x) { return (x * 4 + 255) / 256 * 256; };
+  uint8_t* base = reinterpret_cast<uint8_t*>(ws);
+  float* a_hi = reinterpret_cast<float*>(base);
+  float* a_lo = reinterpret_cast<float*>(base + up(a_elems));
+  float* b_hi = reinterpret_cast<float*>(base + 2 * up(a_elems));
+  float* b_lo = reinterpret_cast<float*>(base + 2 * up(a_elems) + up(b_elems));
+  cudaError_t e = launch_split_tf32(reinterpret_cast<const float*>(g.A), a_hi, a_lo, g.batch, g.M, g.K, g.lda, g.sa, s);
+  if (e != cudaSuccess) return CMPX_ERR_CUDA;
+  const int64_t b_rows = g.b_kmajor ? g.N : g.K, b_cols = g.b_kmajor ? g.K : g.N;
+  e = launch_split_tf32(reinterpret_cast<const float*>(g.B), b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb, s);
+  if (e != cudaSuccess) return CMPX_ERR_CUDA;
+  CUtensorMap tA, tA2, tB, tB2;
+  const uint64_t sa = uint64_t(g.M) * uint64_t(g.K), sb = uint64_t(b_rows) * uint64_t(b_cols);
+  if ((st = encode_3d(&tA, CMPX_F32, a_hi, g.K, g.M, g.batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
+  if ((st = encode_3d(&tA2, CMPX_F32, a_lo, g.K, g.M, g.batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
+  if (g.b_kmajor) {
+    if ((st = encode_3d(&tB, CMPX_F32, b_hi, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
+    if ((st = encode_3d(&tB2, CMPX_F32, b_lo, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
+  } else {
+    if ((st = encode_3d(&tB, CMPX_F32, b_hi, g.N, g.K, g.batch, g.N, sb, 32, 32)) != CMPX_OK) return st;
+    if ((st = encode_3d(&tB2, CMPX_F32, b_lo, g.N, g.K, g.batch, g.N, sb, 32, 32)) != CMPX_OK) return st;
+  }
+  return cuda_status(launch_tc_tf32x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));
+}
+
+int packed_matmul(int dtype, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                  cudaStream_t s) {
+  cmpx_gemm_args a;
+  std::memset(&a, 0, sizeof(a));
+  a.dtype = dtype;
+  a.A = A;
+  a.B = B;
+  a.C = C;
+  a.batch = 1;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.lda = K;
+  a.ldb = N;
+  a.ldc = N;
+  a.b_layout = CMPX_B_KN;
+  return run_gemm(&a, s);
+}
+
+}  // namespace
+
+int* device_error_word() {
+  DeviceState* d = nullptr;
+  return device_state(&d) == CMPX_OK ? d->err_word : nullptr;
+}
+
+}  // namespace cmpx
+
+using namespace cmpx;
+
+extern "C" {
+
+int cmpx_matmul_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cmpx_stream_t stream) {
+  return packed_matmul(CMPX_F16, A, B, C, M, N, K, stream);
+}
+
+int cmpx_matmul_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cmpx_stream_t stream) {
+  return packed_matmul(CMPX_BF16, A, B, C, M, N, K, stream);
+}
+
+int cmpx_matmul_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                    cmpx_stream_t stream) {
+  return packed_matmul(CMPX_F32, A, B, C, M, N, K, stream);
+}
+
+int cmpx_gemm(const cmpx_gemm_args* args, cmpx_stream_t stream) { return run_gemm(args, stream); }
+
+size_t cmpx_gemm_workspace_size(const cmpx_gemm_args* args) {
+  if (validate(args) != CMPX_OK) return 0;
+  if (args->batch == 0 || args->M == 0 || args->N == 0) return 0;
+  DeviceState* d = nullptr;
+  if (device_state(&d) != CMPX_OK) return 0;
+  const Gemm g = to_gemm(args);
+  const int path = choose_path(g, args->path);
+  if (path < 0) return 0;
+  return workspace_for(g, path, d->info);
+}
+
+int cmpx_gemm_select_path(const cmpx_gemm_args* args) {
+  if (validate(args) != CMPX_OK) return -1;
+  const Gemm g = to_gemm(args);
+  return choose_path(g, args->path);
+}
+
+int cmpx_add_bias(int dtype, void* C, const void* bias, int64_t rows, int64_t cols, cmpx_stream_t stream) {
+  if (dtype != CMPX_F16 && dtype != CMPX_BF16 && dtype != CMPX_F32) return CMPX_ERR_INVALID_ARG;
+  if (rows < 0 || cols < 0) return CMPX_ERR_INVALID_ARG;
+  if (rows == 0 || cols == 0) return CMPX_OK;
+  if (C == nullptr || bias == nullptr) return CMPX_ERR_INVALID_ARG;
+  return cuda_status(launch_add_bias(dtype, C, bias, rows, cols, stream));
+}
+
+int cmpx_device_error(int* code) {
+  if (code == nullptr) return CMPX_ERR_INVALID_ARG;
+  *code = 0;
+  int* w = device_error_word();
+  if (w == nullptr) return CMPX_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return CMPX_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return CMPX_ERR_CUDA;
+  if (v != 0) {
+    const int zero = 0;
+    if (cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return CMPX_ERR_CUDA;
+  }
+  *code = v;
+  return CMPX_OK;
+}
+
+const char* cmpx_status_string(int status) {
+  switch (status) {
+    case CMPX_OK: return "ok";
+    case CMPX_ERR_INVALID_ARG: return "invalid argument";
+    case CMPX_ERR_UNSUPPORTED: return "unsupported shape, alignment, path or device";
+    case CMPX_ERR_CUDA: return "CUDA error";
+    case CMPX_ERR_NO_MEMORY: return "out of device memory for workspace";
+    case CMPX_ERR_DEVICE: return "device-side error (bounded wait expired)";
+    case CMPX_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+const char* cmpx_version(void) { return "cmpx 0.1.0 sm_100a"; }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Reference-compatible C++-linkage launchers (same signatures as
+// src/main.cpp:12-19).  Legacy default stream, no return value; a failure is
+// reported on stderr, as the reference's fp32 launcher does
+// (src/cuda/fp32_matmul.cu:260-264).
+static void report(const char* what, int st) {
+  if (st != CMPX_OK) std::fprintf(stderr, "cmpx %s error: %s\n", what, cmpx_status_string(st));
+}
+
+CMPX_API void launch_matmul_fp16(const void* input, const void* weight, void* output, int M, int N, int K) {
+  report("launch_matmul_fp16", cmpx_matmul_f16(input, weight, output, M, N, K, nullptr));
+}
+CMPX_API void launch_matmul_fp32(const float* input, const float* weight, float* output, int M, int N, int K) {
+  report("launch_matmul_fp32", cmpx_matmul_f32(input, weight, output, M, N, K, nullptr));
+}
+CMPX_API void launch_matmul_bf16(const void* input, const void* weight, void* output, int M, int N, int K) {
+  report("launch_matmul_bf16", cmpx_matmul_bf16(input, weight, output, M, N, K, nullptr));
+}
+CMPX_API void launch_add_bias_fp16(void* output, const void* bias, int rows, int cols) {
+  report("launch_add_bias_fp16", cmpx_add_bias(CMPX_F16, output, bias, rows, cols, nullptr));
+}
+CMPX_API void launch_add_bias_fp32(float* output, const float* bias, int rows, int cols) {
+  report("launch_add_bias_fp32", cmpx_add_bias(CMPX_F32, output, bias, rows, cols, nullptr));
+}
+CMPX_API void launch_add_bias_bf16(void* output, const void* bias, int rows, int cols) {
+  report("launch_add_bias_bf16", cmpx_add_bias(CMPX_BF16, output, bias, rows, cols, nullptr));
+}

@@ -1,0 +1,371 @@
+// Swap-AB, stream-K tcgen05 GEMM for skinny M (decode shapes, M <= 64).
+//
+// The reference runs every shape through its 128x128 SIMT tile kernel
+// (src/cuda/fp16_matmul.cu:63-283, bf16: src/cuda/bf16_matmul.cu:51-226);
+// at M = 16 127/128 of each tile is zero padding and the B operand (the
+// weight, hundreds of MB) is streamed by only N/128 CTAs.  Here the product is
+// computed transposed, C^T[N, M] = B^T[N, K] * A^T[K, M]:
+//   * the 128-row MMA operand is a 128-column slab of B (N fills MMA-M),
+//   * the narrow MMA operand is A (MMA-N = M rounded up to 16/32/64),
+// and the (N-tile, k-block) work units are split evenly over one CTA per SM
+// (stream-K), so every SM streams an equal share of B from HBM.  A tile whose
+// k-range is split between CTAs is reduced deterministically: each part
+// writes fp32 partials to a workspace slot, and the last part to arrive
+// (per-tile counter) sums the parts in CTA order, adds the bias, rounds once
+// and stores.  The counters are left at zero for the next launch.
+//
+// Shared-memory operand layouts (128-byte swizzle, written by TMA):
+//   B slab, [K,N] source: 2 chunks of [64 K rows][64 N] (MN-major, LBO 8192, SBO 1024)
+//   B slab, [N,K] source: [128 N rows][64 K]            (K-major, SBO 1024)
+//   A tile            : [MN rows][64 K]                  (K-major, SBO 1024)
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace cmpx {
+namespace {
+
+struct SkParams {
+  void* C;
+  const void* bias;
+  int M, N, K, batch;
+  long long ldc, stride_c;
+  int n_tiles;    // N-tiles per batch entry
+  int kbt;        // k-blocks per tile
+  long long units;  // batch * n_tiles * kbt
+  float* ws;      // [grid][2][MN][128] fp32 partials
+  int* counters;  // [batch * n_tiles][4] (one per epilogue warp quadrant)
+  int* err;
+};
+
+template <int FMT, bool B_KMAJOR, int MN, int STAGES>
+struct SkCfg {
+  static constexpr int BK = 64;
+  static constexpr int SLAB_BYTES = 128 * 128;      // 128 N x 64 K x 2 B
+  static constexpr int ATILE_BYTES = MN * 128;      // MN rows x 64 K x 2 B
+  static constexpr int STAGE_BYTES = SLAB_BYTES + ATILE_BYTES;
+  static constexpr uint32_t TMEM_COLS = (2 * MN) < 32 ? 32 : 2 * MN;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t IDESC = make_idesc(uint32_t(FMT), B_KMAJOR ? 0u : 1u, 0u, 128, MN);
+  static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+};
+
+__device__ __forceinline__ long long unit_begin(long long g, long long U, long long G) { return g * U / G; }
+// CTA owning unit u: the largest g with unit_begin(g) <= u.
+__device__ __forceinline__ long long unit_owner(long long u, long long U, long long G) {
+  return ((u + 1) * G - 1) / U;
+}
+
+__device__ __forceinline__ void record_error(int* err, volatile int* abort, int code) {
+  *abort = 1;
+  atomicCAS(err, 0, code);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ void from_f32(float v, __half* o) { *o = __float2half_rn(v); }
+__device__ __forceinline__ void from_f32(float v, __nv_bfloat16* o) { *o = __float2bfloat16_rn(v); }
+
+template <int FMT, bool B_KMAJOR, int MN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
+                       const SkParams p) {
+  using Cfg = SkCfg<FMT, B_KMAJOR, MN, STAGES>;
+  using T = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const long long G = gridDim.x;
+  const long long U = p.units;
+  const long long u_begin = unit_begin(blockIdx.x, U, G);
+  const long long u_end = unit_begin(blockIdx.x + 1, U, G);
+  const int kbt = p.kbt;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmB);
+      prefetch_tmap(&tmA);
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (long long u = u_begin; u < u_end && ok; ++u) {
+        const long long tile = u / kbt;
+        const int kb = int(u - tile * kbt);
+        const int b = int(tile / p.n_tiles);
+        const int n0 = int(tile - 1LL * b * p.n_tiles) * 128;
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
+          record_error(p.err, abort_flag, kDevTimeoutEmpty);
+          ok = false;
+          break;
+        }
+        uint8_t* sB = smem + size_t(stage) * Cfg::STAGE_BYTES;
+        uint8_t* sA = sB + Cfg::SLAB_BYTES;
+        mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+        const int k0 = kb * Cfg::BK;
+        if (B_KMAJOR) {
+          tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0, b);
+        } else {
+          tma_load_3d(sB, &tmB, &full_bar[stage], n0, k0, b);
+          tma_load_3d(sB + 8192, &tmB, &full_bar[stage], n0 + 64, k0, b);
+        }
+        tma_load_3d(sA, &tmA, &full_bar[stage], k0, 0, b);
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) {
+        const uint32_t n = issued < uint32_t(STAGES) ? issued : uint32_t(STAGES);
+        uint32_t s = stage, ph = phase;
+        volatile int never = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+          if (s == 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          } else {
+            --s;
+          }
+          mbar_wait(&full_bar[s], ph, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int ls = 0;  // local segment counter
+      for (long long u = u_begin; u < u_end && ok; ++ls) {
+        const long long tile = u / kbt;
+        const int kb0 = int(u - tile * kbt);
+        const int kb1 = int(min((long long)kbt, (long long)kb0 + (u_end - u)));
+        u += kb1 - kb0;
+        const int acc = ls & 1;
+        const uint32_t acc_phase = (ls >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag)) {
+          record_error(p.err, abort_flag, kDevTimeoutAccEmpty);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * MN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+            record_error(p.err, abort_flag, kDevTimeoutFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t b_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
+          const uint32_t a_addr = b_addr + Cfg::SLAB_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t slab_desc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
+                                                : make_sdesc_sw128(b_addr + ks * 2048, 8192, 1024);
+            const uint64_t a_desc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
+            mma_f16(d_tmem, slab_desc, a_desc, Cfg::IDESC, (kb != kb0 || ks != 0) ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mma_commit(&acc_full[acc]);
+      }
+      if (!ok) {
+        mma_commit(drain_bar);
+        volatile int never = 0;
+        mbar_wait(drain_bar, 0, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int et = threadIdx.x - 64;  // 0..127, == TMEM lane == n offset in the slab
+    T* C = reinterpret_cast<T*>(p.C);
+    const T* bias = reinterpret_cast<const T*>(p.bias);
+    const long long first_tile = u_begin / kbt;
+    int ls = 0;
+    for (long long u = u_begin; u < u_end; ++ls) {
+      const long long tile = u / kbt;
+      const int kb0 = int(u - tile * kbt);
+      const int kb1 = int(min((long long)kbt, (long long)kb0 + (u_end - u)));
+      u += kb1 - kb0;
+      const int b = int(tile / p.n_tiles);
+      const int n = int(tile - 1LL * b * p.n_tiles) * 128 + et;
+      const int acc = ls & 1;
+      const uint32_t acc_phase = (ls >> 1) & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
+      if (!ok) {
+        if (lane == 0) record_error(p.err, abort_flag, kDevTimeoutAccFull);
+        break;
+      }
+      tc_fence_after();
+      float v[MN];
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * MN);
+#pragma unroll
+      for (int c = 0; c < MN; c += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_row + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[c + i] = __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);  // TMEM slot free; the rest works from registers
+
+      const long long t_u0 = tile * kbt;
+      const long long g_lo = unit_owner(t_u0, U, G);
+      const long long g_hi = unit_owner(t_u0 + kbt - 1, U, G);
+      T* cb = C + size_t(b) * p.stride_c;
+      const float bv = (bias != nullptr && n < p.N) ? to_f32<T>(bias[n]) : 0.0f;
+      if (g_lo == g_hi) {
+        // whole k-range in this CTA: store directly (column n of C^T = C[:, n])
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < MN; ++j)
+            if (j < p.M) from_f32(v[j] + bv, cb + size_t(j) * p.ldc + n);
+        }
+      } else {
+        // Each epilogue warp owns 32 lanes (n values) of the slab and reduces
+        // them independently: per-(tile, quadrant) counters, no CTA barrier.
+        const int slot = (tile == first_tile) ? 0 : 1;
+        float* part = p.ws + ((size_t(blockIdx.x) * 2 + slot) * MN) * 128;
+#pragma unroll
+        for (int j = 0; j < MN; ++j) __stcg(part + j * 128 + et, v[j]);
+        __threadfence();
+        __syncwarp();
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(p.counters + tile * 4 + q, 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == int(g_hi - g_lo)) {
+          __threadfence();
+          float s[MN];
+#pragma unroll
+          for (int j = 0; j < MN; ++j) s[j] = 0.0f;
+          for (long long gg = g_lo; gg <= g_hi; ++gg) {
+            const long long gft = unit_begin(gg, U, G) / kbt;
+            const int sl = (tile == gft) ? 0 : 1;
+            const float* pp = p.ws + ((size_t(gg) * 2 + sl) * MN) * 128;
+#pragma unroll
+            for (int j = 0; j < MN; ++j) s[j] += __ldcg(pp + j * 128 + et);
+          }
+          if (n < p.N) {
+#pragma unroll
+            for (int j = 0; j < MN; ++j)
+              if (j < p.M) from_f32(s[j] + bv, cb + size_t(j) * p.ldc + n);
+          }
+          if (lane == 0) p.counters[tile * 4 + q] = 0;
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int FMT, bool B_KMAJOR, int MN, int STAGES>
+cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
+                           const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  using Cfg = SkCfg<FMT, B_KMAJOR, MN, STAGES>;
+  auto kern = gemm_skinny_kernel<FMT, B_KMAJOR, MN, STAGES>;
+  static_assert(Cfg::SMEM <= 232448, "shared memory budget");
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM));
+  if (e != cudaSuccess) return e;
+  SkParams p;
+  p.C = g.C;
+  p.bias = g.bias;
+  p.M = int(g.M);
+  p.N = int(g.N);
+  p.K = int(g.K);
+  p.batch = int(g.batch);
+  p.ldc = g.ldc;
+  p.stride_c = g.sc;
+  p.n_tiles = int((g.N + 127) / 128);
+  p.kbt = int((g.K + 63) / 64);
+  p.units = 1LL * g.batch * p.n_tiles * p.kbt;
+  const long long grid = p.units < dev.num_sms ? p.units : dev.num_sms;
+  p.ws = reinterpret_cast<float*>(ws);
+  p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + size_t(dev.num_sms) * 2 * 64 * 128 * 4);
+  p.err = dev_err;
+  kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(tB, tA, p);
+  return cudaGetLastError();
+}
+
+template <int FMT, bool B_KMAJOR>
+cudaError_t launch_sk_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
+                         const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  switch (skinny_mn(g.M)) {
+    case 16: return launch_sk_impl<FMT, B_KMAJOR, 16, 8>(g, tB, tA, ws, dev, dev_err, s);
+    case 32: return launch_sk_impl<FMT, B_KMAJOR, 32, 8>(g, tB, tA, ws, dev, dev_err, s);
+    default: return launch_sk_impl<FMT, B_KMAJOR, 64, 8>(g, tB, tA, ws, dev, dev_err, s);
+  }
+}
+
+}  // namespace
+
+int skinny_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+
+// Partials for every CTA (sized for the widest MN so the layout does not
+// depend on M) followed by one counter per tile.
+size_t skinny_workspace_bytes(const Gemm& g, const DeviceInfo& dev) {
+  const size_t parts = size_t(dev.num_sms) * 2 * 64 * 128 * 4;
+  const size_t tiles = size_t(g.batch) * size_t((g.N + 127) / 128);
+  return parts + ((tiles * 4 * sizeof(int) + 255) / 256) * 256;
+}
+
+cudaError_t launch_skinny(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
+                          const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  if (g.dtype == CMPX_F16)
+    return g.b_kmajor ? launch_sk_mn<0, true>(g, tB, tA, ws, dev, dev_err, s)
+                      : launch_sk_mn<0, false>(g, tB, tA, ws, dev, dev_err, s);
+  return g.b_kmajor ? launch_sk_mn<1, true>(g, tB, tA, ws, dev, dev_err, s)
+                    : launch_sk_mn<1, false>(g, tB, tA, ws, dev, dev_err, s);
+}
+
+}  // namespace cmpx

@@ -1,0 +1,445 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+// Replaces the reference's SIMT tile kernels gemm_fp16_ampere_optimized_v3
+// (src/cuda/fp16_matmul.cu:63-283), gemm_bf16_kernel
+// (src/cuda/bf16_matmul.cu:51-226) and gemm_fp32_ga100_kernel
+// (src/cuda/fp32_matmul.cu:31-184).  Same product C = A*B over row-major
+// operands; the arithmetic differs on purpose: fp32 accumulation in TMEM
+// (fp16/bf16) and 3xTF32 (fp32), both more accurate than the reference's
+// half-precision / FMA-free accumulation.
+//
+// CTA layout (192 threads, one CTA per SM, grid = min(tiles, #SMs)):
+//   warp 0      TMA producer: fills a STAGES-deep ring of A/B tiles
+//   warp 1      TMEM allocator + MMA issuer (one thread)
+//   warps 2..5  epilogue: TMEM -> registers -> (+bias) -> global
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the main loop of tile i+1.  Tiles are visited in grouped-M order so the A
+// row-panels and B column-panels of the ~148 tiles in flight stay in L2.
+//
+// Shared-memory operand layouts (128-byte swizzle, written by TMA):
+//   A tile [128 rows][128 B of K]           K-major, SBO = 1024
+//   B tile, [K,N] source: BN/CW chunks of [BK rows][128 B of N], MN-major,
+//           LBO = chunk bytes, SBO = 1024   (CW = 128 B / elem)
+//   B tile, [N,K] source: [BN rows][128 B of K], K-major, SBO = 1024
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace cmpx {
+namespace {
+
+struct TcParams {
+  void* C;
+  const void* bias;
+  int M, N, K, batch;
+  long long ldc, stride_c;
+  int tiles_m, tiles_n, group_m;
+  int* err;
+};
+
+// FMT: 0 = f16, 1 = bf16, 2 = tf32x3 (fp32 in/out)
+template <int FMT, bool B_KMAJOR, int BN_, int STAGES_>
+struct TcCfg {
+  static constexpr int E = FMT == 2 ? 4 : 2;  // input/output element bytes
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int BK = 128 / E;         // one 128-byte swizzle atom of K
+  static constexpr int NOPS = FMT == 2 ? 2 : 1;  // hi (+ lo) copies per operand
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
+  static constexpr int CW = 128 / E;         // N-major chunk width in elements
+  static constexpr int CHUNK_BYTES = BK * 128;
+  static constexpr int KSTEP_BYTES_MN = (32 / E) * 128;  // UMMA_K rows of an MN-major tile
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t IDESC = make_idesc(FMT == 2 ? 2u : uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, BM, BN);
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(B_KMAJOR || BN % CW == 0, "BN must be whole N-major chunks");
+};
+
+__device__ __forceinline__ void decode_tile(int t, const TcParams& p, int& b, int& tm, int& tn) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  b = t / per_batch;
+  const int r = t - b * per_batch;
+  const int gw = p.group_m * p.tiles_n;
+  const int g = r / gw;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.tiles_m - first_m, p.group_m);
+  const int rr = r - g * gw;
+  tm = first_m + rr % gm;
+  tn = rr / gm;
+}
+
+__device__ __forceinline__ void record_error(int* err, volatile int* abort, int code) {
+  *abort = 1;
+  atomicCAS(err, 0, code);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Stores 32 consecutive fp32 accumulator columns of one output row.
+// Full 16-byte groups inside [0, N) use vector stores; a ragged last group
+// falls back to scalar stores.
+template <typename T>
+__device__ __forceinline__ void store_row32(T* crow, const T* bias, int col0, int N, const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int c = col0 + i;
+      if (c < N) v[i] += to_f32<T>(bias[c]);
+    }
+  }
+  if constexpr (sizeof(T) == 2) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int c = col0 + g * 8;
+      if (c + 8 <= N) {
+        uint4 q;
+        q.x = pack2(v[g * 8 + 0], v[g * 8 + 1], (T*)nullptr);
+        q.y = pack2(v[g * 8 + 2], v[g * 8 + 3], (T*)nullptr);
+        q.z = pack2(v[g * 8 + 4], v[g * 8 + 5], (T*)nullptr);
+        q.w = pack2(v[g * 8 + 6], v[g * 8 + 7], (T*)nullptr);
+        *reinterpret_cast<uint4*>(crow + c) = q;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (c + i < N) {
+            if constexpr (std::is_same<T, __half>::value)
+              crow[c + i] = __float2half_rn(v[g * 8 + i]);
+            else
+              crow[c + i] = __float2bfloat16_rn(v[g * 8 + i]);
+          }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const int c = col0 + g * 4;
+      if (c + 4 <= N) {
+        *reinterpret_cast<float4*>(crow + c) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (c + i < N) crow[c + i] = v[g * 4 + i];
+      }
+    }
+  }
+}
+
+template <int FMT, bool B_KMAJOR, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                   const TcParams p) {
+  using Cfg = TcCfg<FMT, B_KMAJOR, BN, STAGES>;
+  using OutT = typename std::conditional<FMT == 0, __half, typename std::conditional<FMT == 1, __nv_bfloat16, float>::type>::type;
+
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzle atoms.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2]
+  uint64_t* drain_bar = acc_empty + 2;       // [1]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int total_tiles = p.tiles_m * p.tiles_n * p.batch;
+  const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      if (FMT == 2) {
+        prefetch_tmap(&tmA2);
+        prefetch_tmap(&tmB2);
+      }
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int b, tm, tn;
+        decode_tile(t, p, b, tm, tn);
+        const int m0 = tm * Cfg::BM, n0 = tn * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
+            record_error(p.err, abort_flag, kDevTimeoutEmpty);
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + size_t(stage) * Cfg::STAGE_BYTES;
+          uint8_t* sB = sA + Cfg::NOPS * Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          const int k0 = kb * Cfg::BK;
+          tma_load_3d(sA, &tmA, &full_bar[stage], k0, m0, b);
+          if (FMT == 2) tma_load_3d(sA + Cfg::A_BYTES, &tmA2, &full_bar[stage], k0, m0, b);
+          if (B_KMAJOR) {
+            tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0, b);
+            if (FMT == 2) tma_load_3d(sB + Cfg::B_BYTES, &tmB2, &full_bar[stage], k0, n0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / Cfg::CW; ++j) {
+              tma_load_3d(sB + j * Cfg::CHUNK_BYTES, &tmB, &full_bar[stage], n0 + j * Cfg::CW, k0, b);
+              if (FMT == 2)
+                tma_load_3d(sB + Cfg::B_BYTES + j * Cfg::CHUNK_BYTES, &tmB2, &full_bar[stage], n0 + j * Cfg::CW,
+                            k0, b);
+            }
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA exits.
+        const uint32_t n = issued < uint32_t(STAGES) ? issued : uint32_t(STAGES);
+        uint32_t s = stage, ph = phase;
+        volatile int never = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+          if (s == 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          } else {
+            --s;
+          }
+          mbar_wait(&full_bar[s], ph, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int lt = 0;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        const uint32_t acc_phase = (lt >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag)) {
+          record_error(p.err, abort_flag, kDevTimeoutAccEmpty);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+            record_error(p.err, abort_flag, kDevTimeoutFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::NOPS * Cfg::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t adesc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
+            const uint64_t bdesc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
+                                            : make_sdesc_sw128(b_addr + ks * Cfg::KSTEP_BYTES_MN,
+                                                               Cfg::CHUNK_BYTES, 1024);
+            const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+            if constexpr (FMT == 2) {
+              const uint64_t adesc_lo = make_sdesc_sw128(a_addr + Cfg::A_BYTES + ks * 32, 16, 1024);
+              const uint64_t bdesc_lo =
+                  B_KMAJOR ? make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * 32, 16, 1024)
+                           : make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * Cfg::KSTEP_BYTES_MN, Cfg::CHUNK_BYTES,
+                                              1024);
+              // small cross terms first, then the dominant hi*hi product
+              mma_tf32(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
+              mma_tf32(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
+              mma_tf32(d_tmem, adesc, bdesc, Cfg::IDESC, 1u);
+            } else {
+              mma_f16(d_tmem, adesc, bdesc, Cfg::IDESC, accum);
+            }
+          }
+          mma_commit(&empty_bar[stage]);  // frees the smem slot once these MMAs retire
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mma_commit(&acc_full[acc]);  // accumulator ready for the epilogue
+      }
+      if (!ok) {
+        // Wait for MMAs in flight before TMEM is released.
+        mma_commit(drain_bar);
+        volatile int never = 0;
+        mbar_wait(drain_bar, 0, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    OutT* C = reinterpret_cast<OutT*>(p.C);
+    const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
+    int lt = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
+      int b, tm, tn;
+      decode_tile(t, p, b, tm, tn);
+      const int acc = lt & 1;
+      const uint32_t acc_phase = (lt >> 1) & 1;
+      // warp-uniform decision: every lane must take part in tcgen05.ld
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
+      if (!ok) {
+        if (lane == 0) record_error(p.err, abort_flag, kDevTimeoutAccFull);
+        break;
+      }
+      tc_fence_after();
+      const int row = tm * Cfg::BM + q * 32 + lane;
+      OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        if (row < p.M) store_row32<OutT>(crow, bias, tn * BN + c * 32, p.N, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int FMT, bool B_KMAJOR, int BN, int STAGES>
+cudaError_t launch_tc_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tA2,
+                           const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  using Cfg = TcCfg<FMT, B_KMAJOR, BN, STAGES>;
+  auto kern = gemm_tc_kernel<FMT, B_KMAJOR, BN, STAGES>;
+  static_assert(Cfg::SMEM <= 232448, "shared memory budget");
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM));
+  if (e != cudaSuccess) return e;
+  TcParams p;
+  p.C = g.C;
+  p.bias = g.bias;
+  p.M = int(g.M);
+  p.N = int(g.N);
+  p.K = int(g.K);
+  p.batch = int(g.batch);
+  p.ldc = g.ldc;
+  p.stride_c = g.sc;
+  p.tiles_m = int((g.M + Cfg::BM - 1) / Cfg::BM);
+  p.tiles_n = int((g.N + BN - 1) / BN);
+  p.group_m = 16;
+  p.err = dev_err;
+  const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
+  const int grid = int(total < dev.num_sms ? total : dev.num_sms);
+  kern<<<grid, 192, Cfg::SMEM, s>>>(tA, tB, tA2, tB2, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_tc_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int bn, const DeviceInfo& dev,
+                          int* dev_err, cudaStream_t s) {
+  (void)bn;
+  if (g.dtype == CMPX_F16) {
+    if (g.b_kmajor) return launch_tc_impl<0, true, 256, 4>(g, tA, tB, tA, tB, dev, dev_err, s);
+    return launch_tc_impl<0, false, 256, 4>(g, tA, tB, tA, tB, dev, dev_err, s);
+  }
+  if (g.b_kmajor) return launch_tc_impl<1, true, 256, 4>(g, tA, tB, tA, tB, dev, dev_err, s);
+  return launch_tc_impl<1, false, 256, 4>(g, tA, tB, tA, tB, dev, dev_err, s);
+}
+
+cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
+                             const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  if (g.b_kmajor) return launch_tc_impl<2, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
+  return launch_tc_impl<2, false, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
+}
+
+// ------------------------------------------------------------------ split
+namespace {
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+__global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict__ hi, float* __restrict__ lo,
+                                  long long rows, long long cols, long long ld, long long sx) {
+  const long long b = blockIdx.y;
+  const long long n = rows * cols;
+  const float* xb = X + b * sx;
+  float* hb = hi + b * n;
+  float* lb = lo + b * n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cols, c = i - r * cols;
+    const float x = xb[r * ld + c];
+    const float h = tf32_rna(x);
+    hb[i] = h;
+    lb[i] = tf32_rna(x - h);
+  }
+}
+}  // namespace
+
+cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
+                              int64_t ld, int64_t sx, cudaStream_t s) {
+  const long long n = rows * cols;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
+  split_tf32_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
+  return cudaGetLastError();
+}
+
+}  // namespace cmpx

@@ -1,0 +1,76 @@
+// Internal interface between the C-ABI dispatcher (cmpx_api.cu) and the
+// kernel translation units.  Not installed; not part of the public ABI.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/cmpx.h"
+
+namespace cmpx {
+
+// A fully resolved batched GEMM: C[b] = A[b] * op(B[b]) (+ bias), row-major.
+//   A    : [M, K] with row stride lda, batch stride sa (elements)
+//   B    : b_kmajor == 0 -> [K, N] row-major (ldb >= N)   (matmul / bmm)
+//          b_kmajor == 1 -> [N, K] row-major (ldb >= K)   (linear weight)
+//   C    : [M, N] with row stride ldc, batch stride sc
+//   bias : optional [N], same dtype as C
+struct Gemm {
+  int dtype;
+  const void* A;
+  const void* B;
+  void* C;
+  const void* bias;
+  int64_t batch, M, N, K;
+  int64_t lda, ldb, ldc;
+  int64_t sa, sb, sc;
+  int b_kmajor;
+};
+
+inline int elem_bytes(int dtype) { return dtype == CMPX_F32 ? 4 : 2; }
+
+// Per-device facts cached by the dispatcher.
+struct DeviceInfo {
+  int num_sms;
+  int max_smem_optin;
+};
+
+// Tensor-core main kernel (fp16 / bf16 inputs, fp32 TMEM accumulate).
+// tA/tB are 3-D TMA maps over A and B (see cmpx_api.cu for box shapes).
+cudaError_t launch_tc_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int bn,
+                          const DeviceInfo& dev, int* dev_err, cudaStream_t s);
+
+// 3xTF32 tensor-core kernel for fp32: tA/tA2 map the tf32 hi/lo splits of A,
+// tB/tB2 those of B.
+cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
+                             const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s);
+
+// Splits fp32 X [batch][rows][cols] (row stride ld, batch stride sx) into
+// packed tf32 hi and lo parts ([batch][rows][cols], contiguous).
+cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
+                              int64_t ld, int64_t sx, cudaStream_t s);
+
+// Swap-AB stream-K kernel for skinny M (M <= 64), fp16/bf16.
+// tBop maps B as the MMA's 128-row operand, tAop maps A as the MMA's
+// narrow operand (box rows = mn).  ws: fp32 partials, counters: per-tile ints
+// that are zero on entry and left zero on exit.
+size_t skinny_workspace_bytes(const Gemm& g, const DeviceInfo& dev);
+int skinny_mn(int64_t M);
+cudaError_t launch_skinny(const Gemm& g, const CUtensorMap& tBop, const CUtensorMap& tAop, void* ws,
+                          const DeviceInfo& dev, int* dev_err, cudaStream_t s);
+
+// CUDA-core fallback for shapes the TMA paths cannot describe.
+cudaError_t launch_simt(const Gemm& g, cudaStream_t s);
+
+// C = bias (broadcast over rows) or 0, used when K == 0.
+cudaError_t launch_fill_bias(const Gemm& g, cudaStream_t s);
+
+// Stand-alone row-broadcast bias add (reference launch_add_bias_* semantics,
+// computed in fp32 and rounded once).
+cudaError_t launch_add_bias(int dtype, void* C, const void* bias, int64_t rows, int64_t cols, cudaStream_t s);
+
+// Device error word (see ptx.cuh DeviceError).
+int* device_error_word();
+
+}  // namespace cmpx

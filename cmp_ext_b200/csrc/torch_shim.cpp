@@ -1,0 +1,211 @@
+// cmpext3-compatible torch operators over the libcmpx C ABI.
+//
+// Mirrors the reference's pybind surface for the matmul path
+// (src/main.cpp:1594-1602): linear(input, weight, bias=None) and
+// bmm(input, mat2), with the same argument names, defaults, TORCH_CHECK
+// messages and output shapes as custom_linear_forward (src/main.cpp:155-256)
+// and custom_bmm_forward (src/main.cpp:273-357).  Adds the 2-D
+// fp16_matmul / bf16_matmul / fp32_matmul(a, b) entry points.
+//
+// Differences from the reference, all of which only turn silent misbehaviour
+// into results or errors:
+//   * linear consumes weight [N, K] directly (no weight.t().contiguous() copy,
+//     src/main.cpp:182) and fuses the bias into the GEMM epilogue;
+//   * bmm is one batched launch instead of a host loop (src/main.cpp:313-351);
+//   * non-CUDA tensors are rejected instead of handing host pointers to a
+//     kernel; dtype mismatches in linear are reported by name;
+//   * launches go to the current torch stream under a device guard, not the
+//     legacy default stream of whichever device is current.
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
+
+#include <cstring>
+#include <vector>
+
+#include "cmpx.h"
+
+namespace {
+
+int dtype_code(at::ScalarType t) {
+  switch (t) {
+    case at::kHalf: return CMPX_F16;
+    case at::kBFloat16: return CMPX_BF16;
+    case at::kFloat: return CMPX_F32;
+    default: return -1;
+  }
+}
+
+void check_status(int st, const char* op) {
+  TORCH_CHECK(st == CMPX_OK, op, " failed: ", cmpx_status_string(st));
+}
+
+cmpx_gemm_args base_args(int dtype) {
+  cmpx_gemm_args a;
+  std::memset(&a, 0, sizeof(a));
+  a.dtype = dtype;
+  a.batch = 1;
+  a.path = CMPX_PATH_AUTO;
+  return a;
+}
+
+cmpx_stream_t current_stream() {
+  return reinterpret_cast<cmpx_stream_t>(at::cuda::getCurrentCUDAStream().stream());
+}
+
+// Test hook: force a kernel path for subsequent calls ("" / "auto", "tc",
+// "skinny", "simt").
+int g_forced_path = CMPX_PATH_AUTO;
+
+void set_path(const std::string& p) {
+  if (p.empty() || p == "auto") g_forced_path = CMPX_PATH_AUTO;
+  else if (p == "tc") g_forced_path = CMPX_PATH_TC;
+  else if (p == "skinny") g_forced_path = CMPX_PATH_SKINNY;
+  else if (p == "simt") g_forced_path = CMPX_PATH_SIMT;
+  else TORCH_CHECK(false, "unknown path '", p, "' (auto, tc, skinny, simt)");
+}
+
+torch::Tensor linear(torch::Tensor input, torch::Tensor weight, c10::optional<torch::Tensor> bias) {
+  TORCH_CHECK(input.dim() >= 2, "Input dim >= 2");
+  TORCH_CHECK(weight.dim() == 2, "Weight dim == 2");
+  TORCH_CHECK(input.device() == weight.device(), "Device mismatch");
+  const int64_t N = weight.size(0);
+  const int64_t K = weight.size(1);
+  TORCH_CHECK(input.size(-1) == K, "Input shape mismatch with Weight");
+  TORCH_CHECK(input.is_cuda(), "cmpext3.linear expects CUDA tensors");
+  TORCH_CHECK(input.scalar_type() == weight.scalar_type(), "Dtype mismatch");
+  int64_t M = 1;
+  for (int64_t i = 0; i + 1 < input.dim(); ++i) M *= input.size(i);
+
+  c10::cuda::CUDAGuard guard(input.device());
+  input = input.contiguous();
+  weight = weight.contiguous();
+  torch::Tensor output = torch::empty({M, N}, input.options());
+  if (N % 2 != 0 && input.scalar_type() == at::kHalf) {
+    TORCH_CHECK(false, "Custom FP16 Kernel requires even Output Channels (N)");
+  }
+  const int dt = dtype_code(input.scalar_type());
+  TORCH_CHECK(dt >= 0, "Unsupported dtype");
+
+  torch::Tensor bias_t;
+  if (bias.has_value() && bias->defined()) {
+    bias_t = *bias;
+    TORCH_CHECK(bias_t.device() == input.device(), "Bias device mismatch");
+    TORCH_CHECK(bias_t.dtype() == input.dtype(), "Bias dtype mismatch");
+    TORCH_CHECK(bias_t.dim() == 1, "Bias must be 1D");
+    TORCH_CHECK(bias_t.size(0) == N, "Bias size mismatch");
+    bias_t = bias_t.contiguous();
+  }
+
+  cmpx_gemm_args a = base_args(dt);
+  a.A = input.data_ptr();
+  a.B = weight.data_ptr();
+  a.C = output.data_ptr();
+  a.bias = bias_t.defined() ? bias_t.data_ptr() : nullptr;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.lda = K;
+  a.ldb = K;
+  a.ldc = N;
+  a.b_layout = CMPX_B_NK;
+  a.path = g_forced_path;
+  check_status(cmpx_gemm(&a, current_stream()), "cmpext3.linear");
+
+  std::vector<int64_t> shape(input.sizes().begin(), input.sizes().end() - 1);
+  shape.push_back(N);
+  return output.view(shape);
+}
+
+torch::Tensor bmm(torch::Tensor input, torch::Tensor mat2) {
+  TORCH_CHECK(input.dim() == 3, "Input must be 3D (B, M, K)");
+  TORCH_CHECK(mat2.dim() == 3, "Mat2 must be 3D (B, K, N)");
+  TORCH_CHECK(input.device() == mat2.device(), "Device mismatch");
+  TORCH_CHECK(input.dtype() == mat2.dtype(), "Dtype mismatch");
+  const int64_t B = input.size(0), M = input.size(1), K = input.size(2);
+  const int64_t N = mat2.size(2);
+  TORCH_CHECK(B == mat2.size(0), "Batch size mismatch");
+  TORCH_CHECK(K == mat2.size(1), "Contracting dimension (K) mismatch");
+  TORCH_CHECK(input.is_cuda(), "cmpext3.bmm expects CUDA tensors");
+
+  c10::cuda::CUDAGuard guard(input.device());
+  input = input.contiguous();
+  mat2 = mat2.contiguous();
+  torch::Tensor output = torch::empty({B, M, N}, input.options());
+  if (N % 2 != 0 && input.scalar_type() == at::kHalf) {
+    TORCH_CHECK(false, "Custom FP16 Kernel requires even Output dim (N)");
+  }
+  const int dt = dtype_code(input.scalar_type());
+  TORCH_CHECK(dt >= 0, "Unsupported dtype for custom bmm");
+
+  cmpx_gemm_args a = base_args(dt);
+  a.A = input.data_ptr();
+  a.B = mat2.data_ptr();
+  a.C = output.data_ptr();
+  a.batch = B;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.lda = K;
+  a.ldb = N;
+  a.ldc = N;
+  a.stride_a = M * K;
+  a.stride_b = K * N;
+  a.stride_c = M * N;
+  a.b_layout = CMPX_B_KN;
+  a.path = g_forced_path;
+  check_status(cmpx_gemm(&a, current_stream()), "cmpext3.bmm");
+  return output;
+}
+
+// a [M, K] @ b [K, N] -> [M, N]: the 2-D form of bmm's semantics, restricted
+// to one dtype.
+torch::Tensor matmul_2d(const torch::Tensor& a_in, const torch::Tensor& b_in, at::ScalarType want, const char* name) {
+  TORCH_CHECK(a_in.dim() == 2, "Input must be 2D (M, K)");
+  TORCH_CHECK(b_in.dim() == 2, "Mat2 must be 2D (K, N)");
+  TORCH_CHECK(a_in.device() == b_in.device(), "Device mismatch");
+  TORCH_CHECK(a_in.dtype() == b_in.dtype(), "Dtype mismatch");
+  TORCH_CHECK(a_in.scalar_type() == want, name, " expects ", c10::toString(want), " tensors, got ",
+              c10::toString(a_in.scalar_type()));
+  const int64_t M = a_in.size(0), K = a_in.size(1), N = b_in.size(1);
+  TORCH_CHECK(K == b_in.size(0), "Contracting dimension (K) mismatch");
+  TORCH_CHECK(a_in.is_cuda(), name, " expects CUDA tensors");
+  c10::cuda::CUDAGuard guard(a_in.device());
+  torch::Tensor a = a_in.contiguous();
+  torch::Tensor b = b_in.contiguous();
+  torch::Tensor c = torch::empty({M, N}, a.options());
+  if (N % 2 != 0 && want == at::kHalf) {
+    TORCH_CHECK(false, "Custom FP16 Kernel requires even Output dim (N)");
+  }
+  cmpx_gemm_args args = base_args(dtype_code(want));
+  args.A = a.data_ptr();
+  args.B = b.data_ptr();
+  args.C = c.data_ptr();
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.lda = K;
+  args.ldb = N;
+  args.ldc = N;
+  args.b_layout = CMPX_B_KN;
+  args.path = g_forced_path;
+  check_status(cmpx_gemm(&args, current_stream()), name);
+  return c;
+}
+
+torch::Tensor fp16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kHalf, "fp16_matmul"); }
+torch::Tensor bf16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kBFloat16, "bf16_matmul"); }
+torch::Tensor fp32_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kFloat, "fp32_matmul"); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("linear", &linear, "y = input @ weight.T + bias (cmpext3.linear)", py::arg("input"), py::arg("weight"),
+        py::arg("bias") = py::none());
+  m.def("bmm", &bmm, "batched matmul (B,M,K) x (B,K,N) (cmpext3.bmm)", py::arg("input"), py::arg("mat2"));
+  m.def("fp16_matmul", &fp16_matmul, "a[M,K] @ b[K,N] in fp16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
+  m.def("bf16_matmul", &bf16_matmul, "a[M,K] @ b[K,N] in bf16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
+  m.def("fp32_matmul", &fp32_matmul, "a[M,K] @ b[K,N] in fp32 (3xTF32)", py::arg("a"), py::arg("b"));
+  m.def("_set_path", &set_path, "force a kernel path for testing: auto, tc, skinny, simt");
+  m.def("_version", []() { return std::string(cmpx_version()); });
+}

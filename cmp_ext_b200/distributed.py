@@ -1,0 +1,93 @@
+"""M-sharded GEMM across the GPUs of one node (one process per GPU).
+
+The reference has no multi-GPU code; this is the partitioning the path admits:
+C = A @ B splits into independent row blocks, so rank r owns rows
+[r0, r1) of A and C while B is replicated.  No data-path collective is needed
+unless the caller wants the full C on every rank, in which case the row
+blocks are all-gathered over NCCL (NVLink / NVSwitch).  Chunked gathering
+(``chunks > 1``) overlaps the all-gather of finished row chunks with the
+GEMM of the next chunk on a second stream.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous, balanced row range [r0, r1) of rank `rank` out of `world`."""
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    base, extra = divmod(M, world)
+    r0 = rank * base + min(rank, extra)
+    return r0, r0 + base + (1 if rank < extra else 0)
+
+
+def default_op(dtype: torch.dtype) -> Callable[[torch.Tensor, torch.Tensor], torch.Tensor]:
+    import cmp_ext_b200 as cx
+
+    return {torch.float16: cx.fp16_matmul, torch.bfloat16: cx.bf16_matmul, torch.float32: cx.fp32_matmul}[dtype]
+
+
+def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = None, gather: bool = False,
+                   chunks: int = 1, group=None, op=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """This rank's rows of A @ B, or (gather=True) the full product on every rank.
+
+    a_shard: this rank's rows of A, as given by ``shard_rows(M, world, rank)``.
+    M: total rows (needed when gathering; defaults to a_shard rows x world,
+       which is right when M divides evenly).
+    chunks: with gather=True, split the shard into this many row chunks and
+       all-gather chunk i while chunk i+1 is being multiplied.
+    op: the per-shard GEMM (defaults to cmp_ext_b200's *_matmul for the dtype;
+       tests on CPU pass torch.matmul).
+    """
+    op = op or default_op(a_shard.dtype)
+    if not gather:
+        return op(a_shard, b)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    M = a_shard.shape[0] * world if M is None else M
+    N = b.shape[1]
+    sizes = [shard_rows(M, world, r)[1] - shard_rows(M, world, r)[0] for r in range(world)]
+    if sizes[rank] != a_shard.shape[0]:
+        raise ValueError(f"rank {rank} holds {a_shard.shape[0]} rows, expected {sizes[rank]}")
+    if out is None:
+        out = torch.empty((M, N), dtype=a_shard.dtype, device=a_shard.device)
+    even = all(s == sizes[0] for s in sizes)
+    if not even:
+        # Ragged shards: gather padded blocks, then compact.
+        rows = max(sizes)
+        local = torch.zeros((rows, N), dtype=a_shard.dtype, device=a_shard.device)
+        local[: sizes[rank]] = op(a_shard, b)
+        buf = torch.empty((world * rows, N), dtype=a_shard.dtype, device=a_shard.device)
+        dist.all_gather_into_tensor(buf, local, group=group)
+        for r in range(world):
+            r0, r1 = shard_rows(M, world, r)
+            out[r0:r1] = buf[r * rows: r * rows + sizes[r]]
+        return out
+    S = sizes[0]
+    chunks = max(1, min(chunks, S))
+    if chunks == 1:
+        dist.all_gather_into_tensor(out, op(a_shard, b), group=group)
+        return out
+    # Chunked: all-gather chunk i (into a staging buffer laid out
+    # [chunk][rank][rows]) while the next chunk computes; then scatter rows
+    # into rank-major order.
+    bounds = [(S * i // chunks, S * (i + 1) // chunks) for i in range(chunks)]
+    parts = [op(a_shard[c0:c1], b) for c0, c1 in bounds[:1]]
+    works, stages = [], []
+    for i, (c0, c1) in enumerate(bounds):
+        stage = torch.empty((world * (c1 - c0), N), dtype=a_shard.dtype, device=a_shard.device)
+        works.append(dist.all_gather_into_tensor(stage, parts[i], group=group, async_op=True))
+        stages.append(stage)
+        if i + 1 < len(bounds):
+            n0, n1 = bounds[i + 1]
+            parts.append(op(a_shard[n0:n1], b))
+    for w in works:
+        w.wait()
+    for (c0, c1), stage in zip(bounds, stages):
+        stage = stage.view(world, c1 - c0, N)
+        out.view(world, S, N)[:, c0:c1] = stage
+    return out

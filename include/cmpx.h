@@ -1,0 +1,144 @@
+/* cmpx.h -- C ABI of the B200 (sm_100a) dense matmul library libcmpx.so.
+ *
+ * Drop-in boundary for the dense matmul path of cmpext3 (eastmoe/cmp_ext).
+ * The reference exposes three C++-linkage launchers that take row-major
+ * device pointers with packed strides and launch on the legacy default
+ * stream, returning nothing:
+ *
+ *   void launch_matmul_fp16(const void* A, const void* B, void* C, int M, int N, int K);
+ *   void launch_matmul_fp32(const float* A, const float* B, float* C, int M, int N, int K);
+ *   void launch_matmul_bf16(const void* A, const void* B, void* C, int M, int N, int K);
+ *   void launch_add_bias_{fp16,fp32,bf16}(void* C, const void* bias, int rows, int cols);
+ *
+ *   (reference src/main.cpp:12-19; definitions src/cuda/fp16_matmul.cu:301-366,
+ *    src/cuda/fp32_matmul.cu:236-287, src/cuda/bf16_matmul.cu:232-317)
+ *
+ * libcmpx.so exports those six symbols unchanged (C++ linkage, same
+ * signatures, same default-stream behaviour) so a binary linked against the
+ * reference resolves against this library, plus the extern "C" entry points
+ * below, which add an explicit stream, explicit strides, batching, a fused
+ * bias and a status code.  Nothing in these signatures is a torch type.
+ *
+ * Semantics (all entry points): C[M,N] = A[M,K] * B[K,N] (+ bias[N]) with
+ * row-major operands.  fp16 / bf16 inputs are multiplied on the tensor cores
+ * with fp32 accumulation and rounded once to the output type.  fp32 inputs
+ * use a 3xTF32 split-precision tensor-core kernel (hi*hi + hi*lo + lo*hi,
+ * fp32 accumulation); shapes the TMA engine cannot describe (row strides that
+ * are not a multiple of 16 bytes, unaligned base pointers) use a CUDA-core
+ * kernel with fp32 FMA accumulation.
+ *
+ * All pointers are device pointers on the current device.  Calls are
+ * asynchronous on `stream` (0 = legacy default stream).  Return value: 0 on
+ * success, otherwise a cmpx_status code; nothing is launched on error.
+ */
+#ifndef CMPX_H_
+#define CMPX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CMPX_API __attribute__((visibility("default")))
+#else
+#define CMPX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* cmpx_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  CMPX_OK = 0,
+  CMPX_ERR_INVALID_ARG = 1, /* null pointer, negative size, stride too small, bad enum */
+  CMPX_ERR_UNSUPPORTED = 2, /* forced path cannot handle this shape / alignment */
+  CMPX_ERR_CUDA = 3,        /* a CUDA runtime/driver call or kernel launch failed */
+  CMPX_ERR_NO_MEMORY = 4,   /* library-managed workspace could not be allocated */
+  CMPX_ERR_DEVICE = 5,      /* a kernel reported a device-side error (bounded wait expired) */
+  CMPX_ERR_WORKSPACE = 6    /* caller workspace smaller than cmpx_gemm_workspace_size() */
+} cmpx_status;
+
+typedef enum { CMPX_F16 = 0, CMPX_BF16 = 1, CMPX_F32 = 2 } cmpx_dtype;
+
+typedef enum {
+  CMPX_B_KN = 0, /* B is [K, N] row-major (matmul / bmm operand, reference layout) */
+  CMPX_B_NK = 1  /* B is [N, K] row-major (nn.Linear weight; no transpose copy) */
+} cmpx_b_layout;
+
+typedef enum {
+  CMPX_PATH_AUTO = 0,
+  CMPX_PATH_TC = 1,     /* tcgen05 persistent tile kernel (fp16/bf16) or 3xTF32 (fp32) */
+  CMPX_PATH_SKINNY = 2, /* swap-AB stream-K tcgen05 kernel, M <= 64, fp16/bf16 */
+  CMPX_PATH_SIMT = 3    /* CUDA-core fallback */
+} cmpx_path;
+
+/* General batched GEMM descriptor.  Strides are in elements. */
+typedef struct {
+  int dtype;              /* cmpx_dtype, same for A, B, C, bias */
+  const void* A;          /* [batch][M][K], row stride lda, batch stride stride_a */
+  const void* B;          /* CMPX_B_KN: [batch][K][N] (ldb >= N); CMPX_B_NK: [batch][N][K] (ldb >= K) */
+  void* C;                /* [batch][M][N], row stride ldc, batch stride stride_c */
+  const void* bias;       /* optional [N] (NULL = none), fused into the epilogue */
+  int64_t batch, M, N, K; /* all >= 0 */
+  int64_t lda, ldb, ldc;
+  int64_t stride_a, stride_b, stride_c;
+  int b_layout;           /* cmpx_b_layout */
+  int path;               /* cmpx_path (AUTO unless a test forces one) */
+  void* workspace;        /* optional caller scratch (device); NULL = library-managed */
+  size_t workspace_bytes;
+} cmpx_gemm_args;
+
+/* Replaces launch_matmul_fp16 (reference src/cuda/fp16_matmul.cu:301-340;
+ * declared src/main.cpp:12).  Packed strides lda=K, ldb=ldc=N. */
+CMPX_API int cmpx_matmul_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                    cmpx_stream_t stream);
+
+/* Replaces launch_matmul_bf16 (reference src/cuda/bf16_matmul.cu:232-254;
+ * declared src/main.cpp:14). */
+CMPX_API int cmpx_matmul_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                     cmpx_stream_t stream);
+
+/* Replaces launch_matmul_fp32 (reference src/cuda/fp32_matmul.cu:236-265;
+ * declared src/main.cpp:13). */
+CMPX_API int cmpx_matmul_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                    cmpx_stream_t stream);
+
+/* Replaces the per-batch launch loop of custom_bmm_forward
+ * (reference src/main.cpp:313-351) and the weight.t().contiguous() +
+ * launch_matmul_* + launch_add_bias_* sequence of custom_linear_forward
+ * (reference src/main.cpp:182-246) with one launch. */
+CMPX_API int cmpx_gemm(const cmpx_gemm_args* args, cmpx_stream_t stream);
+
+/* Scratch bytes cmpx_gemm needs for these args when the caller supplies the
+ * workspace (0 when the chosen path needs none). */
+CMPX_API size_t cmpx_gemm_workspace_size(const cmpx_gemm_args* args);
+
+/* Which path cmpx_gemm would take (cmpx_path value; never AUTO), or -1 for
+ * invalid args. */
+CMPX_API int cmpx_gemm_select_path(const cmpx_gemm_args* args);
+
+/* Replaces launch_add_bias_{fp16,fp32,bf16} (reference
+ * src/cuda/fp16_matmul.cu:357-366, src/cuda/fp32_matmul.cu:272-287,
+ * src/cuda/bf16_matmul.cu:308-317; declared src/main.cpp:17-19).
+ * C[r, c] += bias[c] for every row, computed in fp32 and rounded once; unlike
+ * the reference it is correct for odd (fp16) and non-multiple-of-4 (fp32)
+ * column counts. */
+CMPX_API int cmpx_add_bias(int dtype, void* C, const void* bias, int64_t rows, int64_t cols, cmpx_stream_t stream);
+
+/* Reads and clears the device-side error word of the current device
+ * (synchronises the device).  *code receives the first error a kernel
+ * recorded since the last call (0 = none).  Returns CMPX_OK or CMPX_ERR_CUDA. */
+CMPX_API int cmpx_device_error(int* code);
+
+/* Human-readable name of a cmpx_status value. */
+CMPX_API const char* cmpx_status_string(int status);
+
+/* Library version, e.g. "cmpx 0.1.0 sm_100a". */
+CMPX_API const char* cmpx_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* CMPX_H_ */

@@ -1,0 +1,98 @@
+"""The C ABI boundary without a GPU: the library loads, exports every symbol
+include/cmpx.h declares (plus the reference's six C++ launcher symbols), and
+rejects bad arguments before touching a device; path selection is pure host
+logic."""
+import ctypes
+import subprocess
+
+import pytest
+
+import cabi
+
+REF_LAUNCHERS = [  # reference src/main.cpp:12-19, C++ linkage
+    "_Z18launch_matmul_fp16PKvS0_Pviii",
+    "_Z18launch_matmul_fp32PKfS0_Pfiii",
+    "_Z18launch_matmul_bf16PKvS0_Pviii",
+    "_Z20launch_add_bias_fp16PvPKvii",
+    "_Z20launch_add_bias_fp32PfPKfii",
+    "_Z20launch_add_bias_bf16PvPKvii",
+]
+
+
+def test_header_declares_entry_points():
+    names = cabi.declared_symbols()
+    for want in ("cmpx_matmul_f16", "cmpx_matmul_bf16", "cmpx_matmul_f32", "cmpx_gemm", "cmpx_add_bias",
+                 "cmpx_device_error", "cmpx_gemm_workspace_size", "cmpx_gemm_select_path"):
+        assert want in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = cabi.lib()
+    for name in cabi.declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_reference_launcher_symbols_exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", cabi.LIB_PATH], capture_output=True, text=True).stdout
+    for sym in REF_LAUNCHERS:
+        assert sym in out, sym
+
+
+def test_status_strings_and_version():
+    lib = cabi.lib()
+    assert lib.cmpx_status_string(0) == b"ok"
+    assert lib.cmpx_status_string(cabi.ERR_WORKSPACE) == b"workspace too small"
+    assert lib.cmpx_status_string(99) == b"unknown status"
+    assert b"sm_100a" in lib.cmpx_version()
+
+
+def _args(**kw):
+    a = cabi.GemmArgs()
+    a.dtype, a.batch, a.M, a.N, a.K = cabi.F16, 1, 128, 256, 64
+    a.A, a.B, a.C = 0x100000, 0x200000, 0x300000  # fake, 16-byte aligned; never dereferenced
+    a.lda, a.ldb, a.ldc = 64, 256, 256
+    a.b_layout, a.path = cabi.B_KN, cabi.PATH_AUTO
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw", [dict(dtype=7), dict(M=-1), dict(K=-3), dict(b_layout=5), dict(path=9),
+                                dict(ldc=100), dict(lda=10), dict(ldb=100), dict(C=None), dict(A=None),
+                                dict(stride_a=-1)])
+def test_invalid_args_rejected_before_device(kw):
+    assert cabi.gemm(_args(**kw)) == cabi.ERR_INVALID_ARG
+
+
+def test_null_args_and_empty_problems():
+    assert cabi.lib().cmpx_gemm(None, None) == cabi.ERR_INVALID_ARG
+    assert cabi.gemm(_args(M=0)) == cabi.OK
+    assert cabi.gemm(_args(N=0, C=None)) == cabi.OK
+    assert cabi.gemm(_args(batch=0)) == cabi.OK
+    assert cabi.lib().cmpx_add_bias(0, None, None, 0, 5, None) == cabi.OK
+    assert cabi.lib().cmpx_add_bias(9, None, None, 1, 1, None) == cabi.ERR_INVALID_ARG
+
+
+def sel(**kw):
+    return cabi.lib().cmpx_gemm_select_path(ctypes.byref(_args(**kw)))
+
+
+def test_path_selection():
+    assert sel() == cabi.PATH_TC
+    assert sel(M=16) == cabi.PATH_SKINNY
+    assert sel(M=64) == cabi.PATH_SKINNY
+    assert sel(M=65) == cabi.PATH_TC
+    assert sel(A=0x100002) == cabi.PATH_SIMT           # misaligned base
+    assert sel(N=250, ldb=250, ldc=250) == cabi.PATH_SIMT  # row stride not 16-byte multiple
+    assert sel(b_layout=cabi.B_NK, ldb=64) == cabi.PATH_TC
+    assert sel(K=0) == cabi.PATH_SIMT                  # fill kernel
+    # fp32: 3xTF32 when the packed rows are 16-byte multiples and the problem is not tiny
+    assert sel(dtype=cabi.F32, M=4096, N=4096, K=4096, lda=4096, ldb=4096, ldc=4096) == cabi.PATH_TC
+    assert sel(dtype=cabi.F32, M=257, N=383, K=511, lda=511, ldb=383, ldc=383) == cabi.PATH_SIMT
+    assert sel(dtype=cabi.F32, M=8, N=8, K=8, lda=8, ldb=8, ldc=8) == cabi.PATH_SIMT
+    # forced paths
+    assert sel(path=cabi.PATH_SIMT) == cabi.PATH_SIMT
+    assert sel(path=cabi.PATH_SKINNY) == -1            # M = 128 > 64
+    assert sel(path=cabi.PATH_TC, N=250, ldb=250, ldc=250) == -1
+    assert sel(dtype=cabi.F32, path=cabi.PATH_SKINNY, lda=64, ldb=256, ldc=256) == -1
+    assert sel(dtype=9) == -1

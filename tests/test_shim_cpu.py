@@ -1,0 +1,53 @@
+"""The cmpext3-compatible operators' argument checks (reference messages,
+src/main.cpp:161-170, 196-200, 275-302) -- all raised before any device work,
+so they run on CPU tensors."""
+import pytest
+import torch
+
+import cmp_ext_b200 as cx
+import cmpext3
+
+
+def raises(msg, fn, *a):
+    with pytest.raises(RuntimeError, match=msg):
+        fn(*a)
+
+
+def test_drop_in_module_names():
+    for name in ("linear", "bmm", "fp16_matmul", "bf16_matmul", "fp32_matmul"):
+        assert getattr(cmpext3, name) is getattr(cx, name)
+
+
+def test_linear_checks():
+    w = torch.zeros(4, 8)
+    raises("Input dim >= 2", cx.linear, torch.zeros(8), w)
+    raises("Weight dim == 2", cx.linear, torch.zeros(2, 8), torch.zeros(1, 4, 8))
+    raises("Input shape mismatch with Weight", cx.linear, torch.zeros(2, 7), w)
+    raises("expects CUDA tensors", cx.linear, torch.zeros(2, 8), w)
+
+
+def test_bmm_checks():
+    raises(r"Input must be 3D \(B, M, K\)", cx.bmm, torch.zeros(2, 3), torch.zeros(1, 3, 4))
+    raises(r"Mat2 must be 3D \(B, K, N\)", cx.bmm, torch.zeros(1, 2, 3), torch.zeros(3, 4))
+    raises("Dtype mismatch", cx.bmm, torch.zeros(1, 2, 3), torch.zeros(1, 3, 4, dtype=torch.float16))
+    raises("Batch size mismatch", cx.bmm, torch.zeros(1, 2, 3), torch.zeros(2, 3, 4))
+    raises(r"Contracting dimension \(K\) mismatch", cx.bmm, torch.zeros(1, 2, 3), torch.zeros(1, 5, 4))
+    raises("expects CUDA tensors", cx.bmm, torch.zeros(1, 2, 3), torch.zeros(1, 3, 4))
+
+
+def test_matmul_2d_checks():
+    h = torch.float16
+    raises(r"Input must be 2D \(M, K\)", cx.fp16_matmul, torch.zeros(1, 2, 3, dtype=h), torch.zeros(3, 4, dtype=h))
+    raises(r"Mat2 must be 2D \(K, N\)", cx.fp16_matmul, torch.zeros(2, 3, dtype=h), torch.zeros(3, dtype=h))
+    raises("Dtype mismatch", cx.fp16_matmul, torch.zeros(2, 3, dtype=h), torch.zeros(3, 4))
+    raises("fp16_matmul expects Half tensors", cx.fp16_matmul, torch.zeros(2, 3), torch.zeros(3, 4))
+    raises("bf16_matmul expects BFloat16", cx.bf16_matmul, torch.zeros(2, 3), torch.zeros(3, 4))
+    raises("fp32_matmul expects Float", cx.fp32_matmul, torch.zeros(2, 3, dtype=h), torch.zeros(3, 4, dtype=h))
+    raises(r"Contracting dimension \(K\) mismatch", cx.fp32_matmul, torch.zeros(2, 3), torch.zeros(4, 4))
+    raises("expects CUDA tensors", cx.fp32_matmul, torch.zeros(2, 3), torch.zeros(3, 4))
+
+
+def test_set_path_validation():
+    cx._set_path("auto")
+    with pytest.raises(RuntimeError, match="unknown path"):
+        cx._set_path("fast")

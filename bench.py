@@ -256,7 +256,9 @@ def run_ours(args):
     cfg = CONFIGS[args.config]
     metric, unit = metric_of(cfg)
     r0, r1 = shard_rows(cfg.M, world, rank)
-    m = r1 - r0
+    m = r1 - r0 if args.rows is None else args.rows
+    if args.quick:
+        args.no_e2e = args.no_cpu = True
     op = op_for(cfg.dtype)
 
     # Inputs resident in HBM (drawn on the device, seeded per config).
@@ -281,13 +283,14 @@ def run_ours(args):
 
     stream = torch.cuda.current_stream()
     clock = ClockSampler(local)
-    clock.start()
+    if not args.quick:
+        clock.start()
     t_start = time.perf_counter()
-    for _ in range(max(3, args.warmup)):
+    for _ in range(args.warmup if args.quick else max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
     # keep warming until the clock sampler has produced samples (~0.5 s)
-    while time.perf_counter() - t_start < 0.6:
+    while not args.quick and time.perf_counter() - t_start < 0.6:
         step()
         torch.cuda.synchronize()
 
@@ -320,7 +323,7 @@ def run_ours(args):
 
     # Dominant kernel alone (average launch duration, events on its stream).
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kreps = max(5, min(args.steps, 50))
+    kreps = 1 if args.quick else max(5, min(args.steps, 50))
     launch_ms = []
     for _ in range(kreps):
         if flush is not None:
@@ -332,9 +335,10 @@ def run_ours(args):
         launch_ms.append(k0.elapsed_time(k1))
     launch_ms = statistics.median(launch_ms)
 
-    step_flops = 2.0 * cfg.M * cfg.N * cfg.K  # whole job (all ranks)
+    M_job = cfg.M if args.rows is None else args.rows * world
+    step_flops = 2.0 * M_job * cfg.N * cfg.K  # whole job (all ranks)
     e = torch.empty((), dtype=cfg.dtype).element_size()
-    step_bytes_job = (cfg.M * cfg.K + world * cfg.K * cfg.N + cfg.M * cfg.N) * e
+    step_bytes_job = (M_job * cfg.K + world * cfg.K * cfg.N + M_job * cfg.N) * e
     if unit == "GB/s":
         value = step_bytes_job * args.steps / (ms_gemm / 1e3) / 1e9
     else:
@@ -429,6 +433,9 @@ def main(argv=None):
     ap.add_argument("--chunks", type=int, default=4, help="row chunks for the overlapped gather")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiling mode: only W warm-up + K timed steps (no clock sampling, e2e or CPU legs)")
+    ap.add_argument("--rows", type=int, default=None, help="override this rank's M rows (profiling small cases)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)

@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int et = threadIdx.x - 64;  // 0..127, == TMEM lane == n offset in the slab
+    const int et = q * 32 + lane;  // TMEM lane this thread reads == n offset in the slab
     T* C = reinterpret_cast<T*>(p.C);
     const T* bias = reinterpret_cast<const T*>(p.bias);
     const long long first_tile = u_begin / kbt;

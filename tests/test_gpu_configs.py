@@ -1,0 +1,103 @@
+"""The five configurations at full size.
+
+Each one runs the build's kernel (through the C ABI) and the reference's own
+kernel (oracle/_ref) on the same seeded inputs and checks the contract
+    err(build) <= err(reference) + TOL   (TOL 1e-3 fp16/bf16, 1e-5 fp32)
+with err = max|C - C64| / max|C64| over a deterministic sample of rows (fp64
+ground truth for every row is too slow on the host at 16384 x 8192 x 8192).
+Size-independent properties are checked on the full outputs: M-sharded
+computation reproduces the full product bit for bit, and repeated runs are
+bit-identical.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cabi
+from cmp_ext_b200.workloads import CONFIGS, make_inputs
+from oracle import oracle as o
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 1e-3, torch.bfloat16: 1e-3, torch.float32: 1e-5}
+
+
+def _sample_rows(M, n):
+    if M <= n:
+        return np.arange(M)
+    return np.unique(np.linspace(0, M - 1, n).astype(np.int64))
+
+
+def _run(A, B, path=cabi.PATH_AUTO, rows=None):
+    a = A if rows is None else A[rows[0]:rows[1]]
+    C = torch.empty((a.shape[0], B.shape[1]), dtype=A.dtype, device="cuda")
+    assert cabi.gemm(cabi.gemm_args(a, B, C, path=path)) == cabi.OK
+    torch.cuda.synchronize()
+    return C
+
+
+def _errs(cfg, A, B, C, rows):
+    A64 = A[rows].double().cpu().numpy()
+    B64 = B.double().cpu().numpy()
+    C64 = A64 @ B64
+    err = o.normwise_err(C[rows].double().cpu().numpy(), C64)
+    ref_err = None
+    if o.ref_gpu_available():
+        R = torch.empty_like(C)
+        o.ref_gpu_matmul(cfg.dtype_name, A.data_ptr(), B.data_ptr(), R.data_ptr(), A.shape[0], B.shape[1],
+                         A.shape[1])
+        ref_err = o.normwise_err(R[rows].double().cpu().numpy(), C64)
+    return err, ref_err
+
+
+@pytest.mark.parametrize("cid,nrows", [(2, 256), (3, 96), (4, 16), (5, 96)])
+def test_config_within_reference_error(cuda, cid, nrows):
+    cfg = CONFIGS[cid]
+    A, B = make_inputs(cfg, "cpu", seed=0)
+    A, B = A.cuda(), B.cuda()
+    C = _run(A, B)
+    rows = _sample_rows(cfg.M, nrows)
+    err, ref_err = _errs(cfg, A, B, C, rows)
+    print(f"config{cid}: build err {err:.3e}  reference err {ref_err}")
+    assert ref_err is not None, "oracle/_ref (reference kernels) not built"
+    assert err <= ref_err + TOL[cfg.dtype], (err, ref_err)
+    # the build accumulates in fp32: it should be far more accurate than the reference
+    if cfg.dtype != torch.float32:
+        assert err < ref_err
+
+
+@pytest.mark.parametrize("cid", [3, 5])
+def test_m_sharded_equals_full(cuda, cid):
+    """Config 3/5 are M-sharded over up to 8 GPUs: shard products (rows
+    r0:r1, B replicated) concatenated must equal the full product exactly."""
+    from cmp_ext_b200.distributed import shard_rows
+
+    cfg = CONFIGS[cid]
+    A, B = make_inputs(cfg, "cuda", seed=1)
+    full = _run(A, B)
+    for world in (2, 8):
+        parts = [_run(A, B, rows=shard_rows(cfg.M, world, r)) for r in range(world)]
+        assert torch.equal(torch.cat(parts), full), f"world {world}"
+
+
+def test_config4_decode_deterministic(cuda):
+    cfg = CONFIGS[4]
+    A, B = make_inputs(cfg, "cuda", seed=2)
+    c1, c2 = _run(A, B), _run(A, B)
+    assert torch.equal(c1, c2)
+    tref = (A.float() @ B.float())
+    assert o.normwise_err(c1.double().cpu().numpy(), tref.double().cpu().numpy()) < 2e-3
+
+
+def test_fp32_config5_paths_agree(cuda):
+    """Config 5 on the 3xTF32 tensor-core path and the CUDA-core path: both
+    well inside the fp32 bound, on a row sample."""
+    cfg = CONFIGS[5]
+    A, B = make_inputs(cfg, "cuda", seed=3, m=1024)
+    rows = _sample_rows(1024, 64)
+    C64 = A[rows].double().cpu().numpy() @ B.double().cpu().numpy()
+    for path in (cabi.PATH_TC, cabi.PATH_SIMT):
+        C = _run(A, B, path=path)
+        err = o.normwise_err(C[rows].double().cpu().numpy(), C64)
+        print(f"config5 path {path}: err {err:.3e}")
+        assert err < 5e-6

@@ -23,14 +23,20 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Library-managed device memory, per device, grow-only:
+//   slot 0  scratch: fp32 hi/lo splits of the 3xTF32 path (contents do not
+//           survive between calls)
+//   slot 1  skinny-path workspace: fp32 partials plus per-tile counters that
+//           must be zero on entry; the kernel leaves them zero, and no other
+//           path writes this slot
 struct DeviceState {
   bool init = false;
   int status = CMPX_OK;
   DeviceInfo info{};
   int* err_word = nullptr;
   std::mutex ws_mu;
-  void* ws = nullptr;
-  size_t ws_bytes = 0;
+  void* ws[2] = {nullptr, nullptr};
+  size_t ws_bytes[2] = {0, 0};
 };
 
 DeviceState g_dev[kMaxDevices];
@@ -76,27 +82,28 @@ int device_state(DeviceState** out) {
   return d.status;
 }
 
-// Grow-only library-managed workspace, zero-filled when (re)allocated.  It is
-// shared by every call on the device: concurrent calls on different streams
-// that need scratch must pass their own workspace.
-int library_workspace(DeviceState& d, size_t bytes, void** out) {
+// Grow-only library-managed workspace slot, zero-filled when (re)allocated.
+// A slot is shared by every call on the device: concurrent calls on
+// different streams that need scratch must pass their own workspace.
+int library_workspace(DeviceState& d, int slot, size_t bytes, void** out) {
   std::lock_guard<std::mutex> lk(d.ws_mu);
-  if (d.ws_bytes < bytes) {
-    if (d.ws != nullptr) {
-      cudaDeviceSynchronize();  // earlier launches may still read the old buffer
-      cudaFree(d.ws);
-      d.ws = nullptr;
-      d.ws_bytes = 0;
+  if (d.ws_bytes[slot] < bytes) {
+    if (d.ws[slot] != nullptr) {
+      cudaDeviceSynchronize();  // earlier launches may still use the old buffer
+      cudaFree(d.ws[slot]);
+      d.ws[slot] = nullptr;
+      d.ws_bytes[slot] = 0;
     }
-    size_t want = bytes + bytes / 4;
-    if (cudaMalloc(&d.ws, want) != cudaSuccess) {
+    const size_t want = bytes + bytes / 4;
+    if (cudaMalloc(&d.ws[slot], want) != cudaSuccess) {
       cudaGetLastError();
       return CMPX_ERR_NO_MEMORY;
     }
-    if (cudaMemset(d.ws, 0, want) != cudaSuccess) return CMPX_ERR_CUDA;
-    d.ws_bytes = want;
+    if (cudaMemset(d.ws[slot], 0, want) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
+      return CMPX_ERR_CUDA;
+    d.ws_bytes[slot] = want;
   }
-  *out = d.ws;
+  *out = d.ws[slot];
   return CMPX_OK;
 }
 
@@ -186,11 +193,11 @@ bool tma_ok_16bit(const Gemm& g) {
   return ok(g.A, g.lda, g.sa) && ok(g.B, g.ldb, g.sb) && ok(g.C, g.ldc, g.sc);
 }
 
-// fp32 3xTF32: operands are re-packed by the split pre-pass, so only the
-// packed row lengths (K for A; N or K for B) and C need 16-byte alignment.
+// fp32 3xTF32: operands are re-packed K-major by the split pre-pass, so only
+// the packed row length K and C need 16-byte alignment.
 bool tma_ok_f32(const Gemm& g) {
   const bool a_ok = (g.K * 4) % 16 == 0;
-  const bool b_ok = g.b_kmajor ? (g.K * 4) % 16 == 0 : (g.N * 4) % 16 == 0;
+  const bool b_ok = a_ok;  // B is re-packed K-major ([N][K]) by the split pre-pass
   const bool c_ok = aligned16(g.C) && (g.ldc * 4) % 16 == 0 && (g.batch <= 1 || (g.sc * 4) % 16 == 0);
   return a_ok && b_ok && c_ok;
 }
@@ -248,7 +255,7 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
       if (!aligned16(args->workspace)) return CMPX_ERR_INVALID_ARG;
       ws = args->workspace;
     } else {
-      st = library_workspace(*d, need, &ws);
+      st = library_workspace(*d, path == CMPX_PATH_SKINNY ? 1 : 0, need, &ws);
       if (st != CMPX_OK) return st;
     }
   }
@@ -274,7 +281,9 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
     return cuda_status(launch_tc_f16(g, tA, tB, 256, d->info, d->err_word, s));
   }
 
-  // fp32: split A and B into packed tf32 hi/lo, then 3xTF32 on the tensor cores.
+  // fp32: split A and B into packed tf32 hi/lo, then 3xTF32 on the tensor
+  // cores.  B is always stored K-major ([N][K]) by the pre-pass: a [K,N]
+  // source is transposed while it is split.
   const size_t a_elems = size_t(g.batch) * size_t(g.M) * size_t(g.K);
   const size_t b_elems = size_t(g.batch) * size_t(g.K) * size_t(g.N);
   auto up = [](size_t x) { return (x * 4 + 255) / 256 * 256; };
@@ -283,22 +292,19 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   float* a_lo = reinterpret_cast<float*>(base + up(a_elems));
   float* b_hi = reinterpret_cast<float*>(base + 2 * up(a_elems));
   float* b_lo = reinterpret_cast<float*>(base + 2 * up(a_elems) + up(b_elems));
-  cudaError_t e = launch_split_tf32(reinterpret_cast<const float*>(g.A), a_hi, a_lo, g.batch, g.M, g.K, g.lda, g.sa, s);
+  cudaError_t e = launch_split_tf32(reinterpret_cast<const float*>(g.A), a_hi, a_lo, g.batch, g.M, g.K, g.lda, g.sa,
+                                    false, s);
   if (e != cudaSuccess) return CMPX_ERR_CUDA;
   const int64_t b_rows = g.b_kmajor ? g.N : g.K, b_cols = g.b_kmajor ? g.K : g.N;
-  e = launch_split_tf32(reinterpret_cast<const float*>(g.B), b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb, s);
+  e = launch_split_tf32(reinterpret_cast<const float*>(g.B), b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb,
+                        !g.b_kmajor, s);
   if (e != cudaSuccess) return CMPX_ERR_CUDA;
   CUtensorMap tA, tA2, tB, tB2;
-  const uint64_t sa = uint64_t(g.M) * uint64_t(g.K), sb = uint64_t(b_rows) * uint64_t(b_cols);
+  const uint64_t sa = uint64_t(g.M) * uint64_t(g.K), sb = uint64_t(g.N) * uint64_t(g.K);
   if ((st = encode_3d(&tA, CMPX_F32, a_hi, g.K, g.M, g.batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
   if ((st = encode_3d(&tA2, CMPX_F32, a_lo, g.K, g.M, g.batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
-  if (g.b_kmajor) {
-    if ((st = encode_3d(&tB, CMPX_F32, b_hi, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
-    if ((st = encode_3d(&tB2, CMPX_F32, b_lo, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
-  } else {
-    if ((st = encode_3d(&tB, CMPX_F32, b_hi, g.N, g.K, g.batch, g.N, sb, 32, 32)) != CMPX_OK) return st;
-    if ((st = encode_3d(&tB2, CMPX_F32, b_lo, g.N, g.K, g.batch, g.N, sb, 32, 32)) != CMPX_OK) return st;
-  }
+  if ((st = encode_3d(&tB, CMPX_F32, b_hi, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
+  if ((st = encode_3d(&tB2, CMPX_F32, b_lo, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
   return cuda_status(launch_tc_tf32x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));
 }
 

@@ -21,6 +21,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -40,16 +42,24 @@ struct SkParams {
   int* err;
 };
 
-template <int FMT, bool B_KMAJOR, int MN, int STAGES>
+// NS = number of 128-column sub-slabs per work unit (tile width 128*NS):
+// wider units read longer contiguous runs of each B row.
+template <int FMT, bool B_KMAJOR, int MN, int NS>
 struct SkCfg {
   static constexpr int BK = 64;
-  static constexpr int SLAB_BYTES = 128 * 128;      // 128 N x 64 K x 2 B
+  static constexpr int SUB_BYTES = 128 * 128;       // 128 N x 64 K x 2 B
+  static constexpr int SLAB_BYTES = NS * SUB_BYTES;
   static constexpr int ATILE_BYTES = MN * 128;      // MN rows x 64 K x 2 B
   static constexpr int STAGE_BYTES = SLAB_BYTES + ATILE_BYTES;
-  static constexpr uint32_t TMEM_COLS = (2 * MN) < 32 ? 32 : 2 * MN;
+  static constexpr int STAGES_FIT = (225 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
+  static constexpr int ACC_COLS = NS * MN;          // one accumulator buffer
+  static constexpr uint32_t TMEM_COLS = (2 * ACC_COLS) < 32 ? 32 : 2 * ACC_COLS;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
   static constexpr uint32_t IDESC = make_idesc(uint32_t(FMT), B_KMAJOR ? 0u : 1u, 0u, 128, MN);
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+  static_assert(STAGES >= 2, "pipeline depth");
+  static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
 };
 
 __device__ __forceinline__ long long unit_begin(long long g, long long U, long long G) { return g * U / G; }
@@ -72,11 +82,12 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return
 __device__ __forceinline__ void from_f32(float v, __half* o) { *o = __float2half_rn(v); }
 __device__ __forceinline__ void from_f32(float v, __nv_bfloat16* o) { *o = __float2bfloat16_rn(v); }
 
-template <int FMT, bool B_KMAJOR, int MN, int STAGES>
+template <int FMT, bool B_KMAJOR, int MN, int NS>
 __global__ void __launch_bounds__(192, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
                        const SkParams p) {
-  using Cfg = SkCfg<FMT, B_KMAJOR, MN, STAGES>;
+  using Cfg = SkCfg<FMT, B_KMAJOR, MN, NS>;
+  constexpr int STAGES = Cfg::STAGES;
   using T = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
 
   extern __shared__ uint8_t smem_raw[];
@@ -129,7 +140,7 @@ __global__ void __launch_bounds__(192, 1)
         const long long tile = u / kbt;
         const int kb = int(u - tile * kbt);
         const int b = int(tile / p.n_tiles);
-        const int n0 = int(tile - 1LL * b * p.n_tiles) * 128;
+        const int n0 = int(tile - 1LL * b * p.n_tiles) * (128 * NS);
         if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
           record_error(p.err, abort_flag, kDevTimeoutEmpty);
           ok = false;
@@ -139,11 +150,15 @@ __global__ void __launch_bounds__(192, 1)
         uint8_t* sA = sB + Cfg::SLAB_BYTES;
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
         const int k0 = kb * Cfg::BK;
-        if (B_KMAJOR) {
-          tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0, b);
-        } else {
-          tma_load_3d(sB, &tmB, &full_bar[stage], n0, k0, b);
-          tma_load_3d(sB + 8192, &tmB, &full_bar[stage], n0 + 64, k0, b);
+#pragma unroll
+        for (int sub = 0; sub < NS; ++sub) {
+          uint8_t* dst = sB + sub * Cfg::SUB_BYTES;
+          if (B_KMAJOR) {
+            tma_load_3d(dst, &tmB, &full_bar[stage], k0, n0 + sub * 128, b);
+          } else {
+            tma_load_3d(dst, &tmB, &full_bar[stage], n0 + sub * 128, k0, b);
+            tma_load_3d(dst + 8192, &tmB, &full_bar[stage], n0 + sub * 128 + 64, k0, b);
+          }
         }
         tma_load_3d(sA, &tmA, &full_bar[stage], k0, 0, b);
         ++issued;
@@ -186,7 +201,7 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * MN);
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * Cfg::ACC_COLS);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
             record_error(p.err, abort_flag, kDevTimeoutFull);
@@ -198,10 +213,14 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t a_addr = b_addr + Cfg::SLAB_BYTES;
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t slab_desc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
-                                                : make_sdesc_sw128(b_addr + ks * 2048, 8192, 1024);
             const uint64_t a_desc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
-            mma_f16(d_tmem, slab_desc, a_desc, Cfg::IDESC, (kb != kb0 || ks != 0) ? 1u : 0u);
+#pragma unroll
+            for (int sub = 0; sub < NS; ++sub) {
+              const uint32_t sb = b_addr + sub * Cfg::SUB_BYTES;
+              const uint64_t slab_desc = B_KMAJOR ? make_sdesc_sw128(sb + ks * 32, 16, 1024)
+                                                  : make_sdesc_sw128(sb + ks * 2048, 8192, 1024);
+              mma_f16(d_tmem + sub * MN, slab_desc, a_desc, Cfg::IDESC, (kb != kb0 || ks != 0) ? 1u : 0u);
+            }
           }
           mma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -231,7 +250,7 @@ __global__ void __launch_bounds__(192, 1)
       const int kb1 = int(min((long long)kbt, (long long)kb0 + (u_end - u)));
       u += kb1 - kb0;
       const int b = int(tile / p.n_tiles);
-      const int n = int(tile - 1LL * b * p.n_tiles) * 128 + et;
+      const int nt0 = int(tile - 1LL * b * p.n_tiles) * (128 * NS) + et;  // n of sub-slab 0
       const int acc = ls & 1;
       const uint32_t acc_phase = (ls >> 1) & 1;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
@@ -240,38 +259,47 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      float v[MN];
-      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * MN);
-#pragma unroll
-      for (int c = 0; c < MN; c += 16) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(t_row + c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[c + i] = __uint_as_float(r[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);  // TMEM slot free; the rest works from registers
-
       const long long t_u0 = tile * kbt;
       const long long g_lo = unit_owner(t_u0, U, G);
       const long long g_hi = unit_owner(t_u0 + kbt - 1, U, G);
+      const bool whole = g_lo == g_hi;  // whole k-range of the tile in this CTA
+      const int slot = (tile == first_tile) ? 0 : 1;
       T* cb = C + size_t(b) * p.stride_c;
-      const float bv = (bias != nullptr && n < p.N) ? to_f32<T>(bias[n]) : 0.0f;
-      if (g_lo == g_hi) {
-        // whole k-range in this CTA: store directly (column n of C^T = C[:, n])
-        if (n < p.N) {
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * Cfg::ACC_COLS);
+#pragma unroll 1
+      for (int sub = 0; sub < NS; ++sub) {
+        float v[MN];
 #pragma unroll
-          for (int j = 0; j < MN; ++j)
-            if (j < p.M) from_f32(v[j] + bv, cb + size_t(j) * p.ldc + n);
+        for (int c = 0; c < MN; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_row + sub * MN + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[c + i] = __uint_as_float(r[i]);
         }
-      } else {
-        // Each epilogue warp owns 32 lanes (n values) of the slab and reduces
-        // them independently: per-(tile, quadrant) counters, no CTA barrier.
-        const int slot = (tile == first_tile) ? 0 : 1;
-        float* part = p.ws + ((size_t(blockIdx.x) * 2 + slot) * MN) * 128;
+        const int n = nt0 + sub * 128;
+        if (whole) {
+          // column n of C^T is C[:, n]: lanes write consecutive n (coalesced)
+          if (n < p.N) {
+            const float bv = bias != nullptr ? to_f32<T>(bias[n]) : 0.0f;
 #pragma unroll
-        for (int j = 0; j < MN; ++j) __stcg(part + j * 128 + et, v[j]);
+            for (int j = 0; j < MN; ++j)
+              if (j < p.M) from_f32(v[j] + bv, cb + size_t(j) * p.ldc + n);
+          }
+        } else {
+          float* part = p.ws + (((size_t(blockIdx.x) * 2 + slot) * NS + sub) * MN) * 128;
+#pragma unroll
+          for (int j = 0; j < MN; ++j) __stcg(part + j * 128 + et, v[j]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);  // TMEM buffer free for the segment after next
+
+      if (!whole) {
+        // Each epilogue warp owns 32 lanes (n values) of every sub-slab and
+        // reduces them independently: per-(tile, quadrant) counters, no CTA
+        // barrier.  The last of the tile's parts to arrive sums all parts in
+        // CTA order (deterministic), adds the bias, rounds once and stores.
         __threadfence();
         __syncwarp();
         int prev = 0;
@@ -279,20 +307,25 @@ __global__ void __launch_bounds__(192, 1)
         prev = __shfl_sync(0xffffffffu, prev, 0);
         if (prev == int(g_hi - g_lo)) {
           __threadfence();
-          float s[MN];
+#pragma unroll 1
+          for (int sub = 0; sub < NS; ++sub) {
+            float acc_s[MN];
 #pragma unroll
-          for (int j = 0; j < MN; ++j) s[j] = 0.0f;
-          for (long long gg = g_lo; gg <= g_hi; ++gg) {
-            const long long gft = unit_begin(gg, U, G) / kbt;
-            const int sl = (tile == gft) ? 0 : 1;
-            const float* pp = p.ws + ((size_t(gg) * 2 + sl) * MN) * 128;
+            for (int j = 0; j < MN; ++j) acc_s[j] = 0.0f;
+            for (long long gg = g_lo; gg <= g_hi; ++gg) {
+              const long long gft = unit_begin(gg, U, G) / kbt;
+              const int sl = (tile == gft) ? 0 : 1;
+              const float* pp = p.ws + (((size_t(gg) * 2 + sl) * NS + sub) * MN) * 128;
 #pragma unroll
-            for (int j = 0; j < MN; ++j) s[j] += __ldcg(pp + j * 128 + et);
-          }
-          if (n < p.N) {
+              for (int j = 0; j < MN; ++j) acc_s[j] += __ldcg(pp + j * 128 + et);
+            }
+            const int n = nt0 + sub * 128;
+            if (n < p.N) {
+              const float bv = bias != nullptr ? to_f32<T>(bias[n]) : 0.0f;
 #pragma unroll
-            for (int j = 0; j < MN; ++j)
-              if (j < p.M) from_f32(s[j] + bv, cb + size_t(j) * p.ldc + n);
+              for (int j = 0; j < MN; ++j)
+                if (j < p.M) from_f32(acc_s[j] + bv, cb + size_t(j) * p.ldc + n);
+            }
           }
           if (lane == 0) p.counters[tile * 4 + q] = 0;
         }
@@ -309,11 +342,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int FMT, bool B_KMAJOR, int MN, int STAGES>
+template <int FMT, bool B_KMAJOR, int MN, int NS>
 cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
                            const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
-  using Cfg = SkCfg<FMT, B_KMAJOR, MN, STAGES>;
-  auto kern = gemm_skinny_kernel<FMT, B_KMAJOR, MN, STAGES>;
+  using Cfg = SkCfg<FMT, B_KMAJOR, MN, NS>;
+  auto kern = gemm_skinny_kernel<FMT, B_KMAJOR, MN, NS>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM));
   if (e != cudaSuccess) return e;
@@ -326,24 +359,34 @@ cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorM
   p.batch = int(g.batch);
   p.ldc = g.ldc;
   p.stride_c = g.sc;
-  p.n_tiles = int((g.N + 127) / 128);
+  p.n_tiles = int((g.N + 128 * NS - 1) / (128 * NS));
   p.kbt = int((g.K + 63) / 64);
   p.units = 1LL * g.batch * p.n_tiles * p.kbt;
   const long long grid = p.units < dev.num_sms ? p.units : dev.num_sms;
   p.ws = reinterpret_cast<float*>(ws);
-  p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + size_t(dev.num_sms) * 2 * 64 * 128 * 4);
+  p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + skinny_partials_bytes(dev, NS, MN));
   p.err = dev_err;
   kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(tB, tA, p);
   return cudaGetLastError();
+}
+
+template <int FMT, bool B_KMAJOR, int MN>
+cudaError_t launch_sk_ns(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
+                         const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  switch (skinny_ns(g, dev)) {
+    case 4: return launch_sk_impl<FMT, B_KMAJOR, MN, 4>(g, tB, tA, ws, dev, dev_err, s);
+    case 2: return launch_sk_impl<FMT, B_KMAJOR, MN, 2>(g, tB, tA, ws, dev, dev_err, s);
+    default: return launch_sk_impl<FMT, B_KMAJOR, MN, 1>(g, tB, tA, ws, dev, dev_err, s);
+  }
 }
 
 template <int FMT, bool B_KMAJOR>
 cudaError_t launch_sk_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
                          const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
   switch (skinny_mn(g.M)) {
-    case 16: return launch_sk_impl<FMT, B_KMAJOR, 16, 8>(g, tB, tA, ws, dev, dev_err, s);
-    case 32: return launch_sk_impl<FMT, B_KMAJOR, 32, 8>(g, tB, tA, ws, dev, dev_err, s);
-    default: return launch_sk_impl<FMT, B_KMAJOR, 64, 8>(g, tB, tA, ws, dev, dev_err, s);
+    case 16: return launch_sk_ns<FMT, B_KMAJOR, 16>(g, tB, tA, ws, dev, dev_err, s);
+    case 32: return launch_sk_ns<FMT, B_KMAJOR, 32>(g, tB, tA, ws, dev, dev_err, s);
+    default: return launch_sk_ns<FMT, B_KMAJOR, 64>(g, tB, tA, ws, dev, dev_err, s);
   }
 }
 
@@ -351,12 +394,36 @@ cudaError_t launch_sk_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap
 
 int skinny_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-// Partials for every CTA (sized for the widest MN so the layout does not
-// depend on M) followed by one counter per tile.
+// Sub-slabs per work unit: the widest of 4 / 2 / 1 that leaves every CTA at
+// least four units and pads N by at most 1/8.  CMPX_SKINNY_NS=1|2|4 overrides
+// (tuning experiments).
+int skinny_ns(const Gemm& g, const DeviceInfo& dev) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* e = std::getenv("CMPX_SKINNY_NS");
+    forced = 0;
+    if (e != nullptr && (e[0] == '1' || e[0] == '2' || e[0] == '4') && e[1] == 0) forced = e[0] - '0';
+  }
+  if (forced > 0) return forced;
+  const int64_t kbt = (g.K + 63) / 64;
+  for (int ns : {4, 2}) {
+    const int64_t w = 128 * ns;
+    const int64_t tiles = (g.N + w - 1) / w;
+    const int64_t pad = tiles * w - g.N;
+    if (pad * 8 <= g.N && g.batch * tiles * kbt >= 4LL * dev.num_sms) return ns;
+  }
+  return 1;
+}
+
+size_t skinny_partials_bytes(const DeviceInfo& dev, int ns, int mn) {
+  return size_t(dev.num_sms) * 2 * size_t(ns) * size_t(mn) * 128 * 4;
+}
+
+// fp32 partials for every CTA, then one counter per (tile, epilogue warp).
 size_t skinny_workspace_bytes(const Gemm& g, const DeviceInfo& dev) {
-  const size_t parts = size_t(dev.num_sms) * 2 * 64 * 128 * 4;
-  const size_t tiles = size_t(g.batch) * size_t((g.N + 127) / 128);
-  return parts + ((tiles * 4 * sizeof(int) + 255) / 256) * 256;
+  const int ns = skinny_ns(g, dev), mn = skinny_mn(g.M);
+  const size_t tiles = size_t(g.batch) * size_t((g.N + 128 * ns - 1) / (128 * ns));
+  return skinny_partials_bytes(dev, ns, mn) + ((tiles * 4 * sizeof(int) + 255) / 256) * 256;
 }
 
 cudaError_t launch_skinny(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,

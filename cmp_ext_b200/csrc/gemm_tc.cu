@@ -59,6 +59,9 @@ struct TcCfg {
   static constexpr uint32_t IDESC = make_idesc(FMT == 2 ? 2u : uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, BM, BN);
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert(B_KMAJOR || BN % CW == 0, "BN must be whole N-major chunks");
+  // An MN-major tf32 operand needs the 128B swizzle with 32B atoms; the
+  // split pre-pass stores fp32 B K-major instead, so that form is not built.
+  static_assert(FMT != 2 || B_KMAJOR, "3xTF32 takes B K-major");
 };
 
 __device__ __forceinline__ void decode_tile(int t, const TcParams& p, int& b, int& tm, int& tn) {
@@ -402,8 +405,7 @@ cudaError_t launch_tc_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMa
 
 cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
                              const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
-  if (g.b_kmajor) return launch_tc_impl<2, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
-  return launch_tc_impl<2, false, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
+  return launch_tc_impl<2, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
 }
 
 // ------------------------------------------------------------------ split
@@ -429,10 +431,48 @@ __global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict
     lb[i] = tf32_rna(x - h);
   }
 }
+
+// Same split, writing the transpose ([cols][rows]) through a 32x32 shared
+// tile so both the reads and the writes are coalesced.
+__global__ void split_tf32_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
+                                            float* __restrict__ lo, long long rows, long long cols, long long ld,
+                                            long long sx) {
+  __shared__ float th[32][33];
+  __shared__ float tl[32][33];
+  const long long b = blockIdx.z;
+  const float* xb = X + b * sx;
+  float* hb = hi + b * rows * cols;
+  float* lb = lo + b * rows * cols;
+  const long long r0 = (long long)blockIdx.y * 32, c0 = (long long)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const long long r = r0 + i, c = c0 + threadIdx.x;
+    float h = 0.0f, l = 0.0f;
+    if (r < rows && c < cols) {
+      const float x = xb[r * ld + c];
+      h = tf32_rna(x);
+      l = tf32_rna(x - h);
+    }
+    th[i][threadIdx.x] = h;
+    tl[i][threadIdx.x] = l;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const long long c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) {
+      hb[c * rows + r] = th[threadIdx.x][i];
+      lb[c * rows + r] = tl[threadIdx.x][i];
+    }
+  }
+}
 }  // namespace
 
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
-                              int64_t ld, int64_t sx, cudaStream_t s) {
+                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
+  if (transpose) {
+    const dim3 grid{unsigned((cols + 31) / 32), unsigned((rows + 31) / 32), unsigned(batch)};
+    split_tf32_transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(X, hi, lo, rows, cols, ld, sx);
+    return cudaGetLastError();
+  }
   const long long n = rows * cols;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;

@@ -42,21 +42,24 @@ cudaError_t launch_tc_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMa
                           const DeviceInfo& dev, int* dev_err, cudaStream_t s);
 
 // 3xTF32 tensor-core kernel for fp32: tA/tA2 map the tf32 hi/lo splits of A,
-// tB/tB2 those of B.
+// tB/tB2 those of B, both packed K-major (B as [N][K]).
 cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
                              const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s);
 
 // Splits fp32 X [batch][rows][cols] (row stride ld, batch stride sx) into
-// packed tf32 hi and lo parts ([batch][rows][cols], contiguous).
+// packed tf32 hi and lo parts: [batch][rows][cols] contiguous, or with
+// transpose = true [batch][cols][rows] contiguous.
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
-                              int64_t ld, int64_t sx, cudaStream_t s);
+                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s);
 
 // Swap-AB stream-K kernel for skinny M (M <= 64), fp16/bf16.
 // tBop maps B as the MMA's 128-row operand, tAop maps A as the MMA's
 // narrow operand (box rows = mn).  ws: fp32 partials, counters: per-tile ints
 // that are zero on entry and left zero on exit.
 size_t skinny_workspace_bytes(const Gemm& g, const DeviceInfo& dev);
+size_t skinny_partials_bytes(const DeviceInfo& dev, int ns, int mn);
 int skinny_mn(int64_t M);
+int skinny_ns(const Gemm& g, const DeviceInfo& dev);
 cudaError_t launch_skinny(const Gemm& g, const CUtensorMap& tBop, const CUtensorMap& tAop, void* ws,
                           const DeviceInfo& dev, int* dev_err, cudaStream_t s);
 

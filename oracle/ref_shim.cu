@@ -13,11 +13,27 @@ void launch_matmul_bf16(const void* input, const void* weight, void* output, int
 
 // dtype: 0 = fp16, 1 = bf16, 2 = fp32.  Launches on the legacy default stream
 // (as the reference does), waits for completion, returns the cudaError_t.
+// The reference's fp16 launcher also sets a persisting-L2 access window over
+// all of B (src/cuda/fp16_matmul.cu:289-299, 333-335) and ignores the result;
+// when B is larger than the device's maximum window that call fails with
+// cudaErrorInvalidValue, which the reference never observes, so it is
+// cleared here too (the kernel launch itself is checked separately).
 extern "C" __attribute__((visibility("default"))) int ref_matmul(int dtype, const void* A, const void* B, void* C,
                                                                   int M, int N, int K) {
   cudaGetLastError();
-  if (dtype == 0) launch_matmul_fp16(A, B, C, M, N, K);
-  else if (dtype == 1) launch_matmul_bf16(A, B, C, M, N, K);
+  if (dtype == 0) {
+    int dev = 0, max_window = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, dev);
+    if (static_cast<long long>(K) * N * 2 > max_window) {
+      launch_matmul_fp16(A, B, C, M, N, K);
+      cudaError_t e = cudaDeviceSynchronize();
+      cudaError_t last = cudaGetLastError();
+      if (e != cudaSuccess) return int(e);
+      return (last == cudaErrorInvalidValue || last == cudaSuccess) ? 0 : int(last);
+    }
+    launch_matmul_fp16(A, B, C, M, N, K);
+  } else if (dtype == 1) launch_matmul_bf16(A, B, C, M, N, K);
   else launch_matmul_fp32(static_cast<const float*>(A), static_cast<const float*>(B), static_cast<float*>(C), M, N, K);
   cudaError_t e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaGetLastError();

@@ -19,7 +19,9 @@ pytestmark = pytest.mark.gpu
 TOL = {torch.float16: 1e-3, torch.bfloat16: 1e-3, torch.float32: 1e-5}
 # fp32-accumulating kernels land near output rounding; these are generous
 # bounds on the distance to a torch fp32 reference of the same product.
-VS_TORCH = {torch.float16: 2e-3, torch.bfloat16: 1.6e-2, torch.float32: 1e-5}
+# (torch's CPU fp32 matmul carries its own rounding error at large K, hence
+# the looser fp32 figure; the fp64 bound below is the real check).
+VS_TORCH = {torch.float16: 2e-3, torch.bfloat16: 1.6e-2, torch.float32: 1e-4}
 KIND = {torch.float16: "f16", torch.bfloat16: "bf16", torch.float32: "f32"}
 
 

@@ -21,20 +21,30 @@ import torch  # noqa: F401  (loads libtorch / c10 before the shim)
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcmpx.so")
 
-try:
-    from . import _cmpext3 as _ext  # type: ignore[attr-defined]
-except ImportError as e:  # pragma: no cover - exercised only on unbuilt trees
-    raise ImportError(
-        "cmp_ext_b200 native extension is not built; run `python -m cmp_ext_b200.build` "
-        f"(or __graft_entry__.build()) first: {e}"
-    ) from e
+_OPS = ("linear", "bmm", "fp16_matmul", "bf16_matmul", "fp32_matmul", "_set_path", "version")
 
-linear = _ext.linear
-bmm = _ext.bmm
-fp16_matmul = _ext.fp16_matmul
-bf16_matmul = _ext.bf16_matmul
-fp32_matmul = _ext.fp32_matmul
-_set_path = _ext._set_path
-version = _ext._version
+
+def _load_ext():
+    try:
+        from . import _cmpext3  # type: ignore[attr-defined]
+    except ImportError as e:
+        raise ImportError(
+            "cmp_ext_b200 native extension is not built; run `python -m cmp_ext_b200.build` "
+            f"(or __graft_entry__.build()) first: {e}"
+        ) from e
+    return _cmpext3
+
+
+def __getattr__(name):
+    # The operators resolve on first use so that `cmp_ext_b200.build` can be
+    # imported (and run) before the extension exists.  A missing extension is
+    # an ImportError, never a fallback.
+    if name in _OPS:
+        ext = _load_ext()
+        value = getattr(ext, "_version" if name == "version" else name)
+        globals()[name] = value
+        return value
+    raise AttributeError(f"module 'cmp_ext_b200' has no attribute {name!r}")
+
 
 __all__ = ["linear", "bmm", "fp16_matmul", "bf16_matmul", "fp32_matmul", "LIB_PATH", "version"]

@@ -202,7 +202,7 @@ bool tma_ok_f32(const Gemm& g) {
   return a_ok && b_ok && c_ok;
 }
 
-int choose_path(const Gemm& g, int requested) {
+int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
   int forced = requested != CMPX_PATH_AUTO ? requested : env_forced_path();
   if (g.K == 0) return CMPX_PATH_SIMT;  // fill kernel
   if (g.dtype == CMPX_F32) {
@@ -215,10 +215,14 @@ int choose_path(const Gemm& g, int requested) {
   }
   const bool ok = tma_ok_16bit(g);
   if (forced == CMPX_PATH_TC) return ok ? CMPX_PATH_TC : -1;
-  if (forced == CMPX_PATH_SKINNY) return (ok && g.M <= 64) ? CMPX_PATH_SKINNY : -1;
+  // The skinny path's counter region holds kSkinnyMaxTiles tiles; without
+  // device facts (host-only path queries) assume the narrowest units.
+  const int64_t sk_tiles = dev != nullptr ? skinny_tiles(g, *dev) : g.batch * ((g.N + 127) / 128);
+  const bool sk_ok = ok && g.M <= 64 && sk_tiles <= kSkinnyMaxTiles;
+  if (forced == CMPX_PATH_SKINNY) return sk_ok ? CMPX_PATH_SKINNY : -1;
   if (forced == CMPX_PATH_SIMT) return CMPX_PATH_SIMT;
   if (!ok) return CMPX_PATH_SIMT;
-  return g.M <= 64 ? CMPX_PATH_SKINNY : CMPX_PATH_TC;
+  return sk_ok ? CMPX_PATH_SKINNY : CMPX_PATH_TC;
 }
 
 size_t f32_split_bytes(const Gemm& g) {
@@ -242,7 +246,7 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   st = device_state(&d);
   if (st != CMPX_OK) return st;
   const Gemm g = to_gemm(args);
-  const int path = choose_path(g, args->path);
+  const int path = choose_path(g, args->path, &d->info);
   if (path < 0) return CMPX_ERR_UNSUPPORTED;
   if (g.K == 0) return cuda_status(launch_fill_bias(g, s));
   if (path == CMPX_PATH_SIMT) return cuda_status(launch_simt(g, s));
@@ -361,7 +365,7 @@ size_t cmpx_gemm_workspace_size(const cmpx_gemm_args* args) {
   DeviceState* d = nullptr;
   if (device_state(&d) != CMPX_OK) return 0;
   const Gemm g = to_gemm(args);
-  const int path = choose_path(g, args->path);
+  const int path = choose_path(g, args->path, &d->info);
   if (path < 0) return 0;
   return workspace_for(g, path, d->info);
 }
@@ -369,7 +373,7 @@ size_t cmpx_gemm_workspace_size(const cmpx_gemm_args* args) {
 int cmpx_gemm_select_path(const cmpx_gemm_args* args) {
   if (validate(args) != CMPX_OK) return -1;
   const Gemm g = to_gemm(args);
-  return choose_path(g, args->path);
+  return choose_path(g, args->path, nullptr);
 }
 
 int cmpx_add_bias(int dtype, void* C, const void* bias, int64_t rows, int64_t cols, cmpx_stream_t stream) {

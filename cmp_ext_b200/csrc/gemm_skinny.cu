@@ -42,17 +42,19 @@ struct SkParams {
   int* err;
 };
 
-// NS = number of 128-column sub-slabs per work unit (tile width 128*NS):
-// wider units read longer contiguous runs of each B row.
+// NS = number of 128-column sub-slabs per work unit (tile width 128*NS).
+// Each pipeline stage holds one sub-slab (and a copy of the A tile), so the
+// stage size -- and with it the pipeline depth -- does not depend on NS,
+// while a CTA's consecutive stages walk NS*256 contiguous bytes of each B row
+// ([K,N] layout) before moving down to the next k-block.
 template <int FMT, bool B_KMAJOR, int MN, int NS>
 struct SkCfg {
   static constexpr int BK = 64;
   static constexpr int SUB_BYTES = 128 * 128;       // 128 N x 64 K x 2 B
-  static constexpr int SLAB_BYTES = NS * SUB_BYTES;
   static constexpr int ATILE_BYTES = MN * 128;      // MN rows x 64 K x 2 B
-  static constexpr int STAGE_BYTES = SLAB_BYTES + ATILE_BYTES;
+  static constexpr int STAGE_BYTES = SUB_BYTES + ATILE_BYTES;
   static constexpr int STAGES_FIT = (225 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
+  static constexpr int STAGES = STAGES_FIT > 16 ? 16 : STAGES_FIT;
   static constexpr int ACC_COLS = NS * MN;          // one accumulator buffer
   static constexpr uint32_t TMEM_COLS = (2 * ACC_COLS) < 32 ? 32 : 2 * ACC_COLS;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
@@ -141,30 +143,28 @@ __global__ void __launch_bounds__(192, 1)
         const int kb = int(u - tile * kbt);
         const int b = int(tile / p.n_tiles);
         const int n0 = int(tile - 1LL * b * p.n_tiles) * (128 * NS);
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
-          record_error(p.err, abort_flag, kDevTimeoutEmpty);
-          ok = false;
-          break;
-        }
-        uint8_t* sB = smem + size_t(stage) * Cfg::STAGE_BYTES;
-        uint8_t* sA = sB + Cfg::SLAB_BYTES;
-        mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
         const int k0 = kb * Cfg::BK;
-#pragma unroll
-        for (int sub = 0; sub < NS; ++sub) {
-          uint8_t* dst = sB + sub * Cfg::SUB_BYTES;
-          if (B_KMAJOR) {
-            tma_load_3d(dst, &tmB, &full_bar[stage], k0, n0 + sub * 128, b);
-          } else {
-            tma_load_3d(dst, &tmB, &full_bar[stage], n0 + sub * 128, k0, b);
-            tma_load_3d(dst + 8192, &tmB, &full_bar[stage], n0 + sub * 128 + 64, k0, b);
+        for (int sub = 0; sub < NS && ok; ++sub) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
+            record_error(p.err, abort_flag, kDevTimeoutEmpty);
+            ok = false;
+            break;
           }
-        }
-        tma_load_3d(sA, &tmA, &full_bar[stage], k0, 0, b);
-        ++issued;
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
+          uint8_t* sB = smem + size_t(stage) * Cfg::STAGE_BYTES;
+          uint8_t* sA = sB + Cfg::SUB_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          if (B_KMAJOR) {
+            tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0 + sub * 128, b);
+          } else {
+            tma_load_3d(sB, &tmB, &full_bar[stage], n0 + sub * 128, k0, b);
+            tma_load_3d(sB + 8192, &tmB, &full_bar[stage], n0 + sub * 128 + 64, k0, b);
+          }
+          tma_load_3d(sA, &tmA, &full_bar[stage], k0, 0, b);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
       }
       if (!ok) {
@@ -202,30 +202,28 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * Cfg::ACC_COLS);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
-            record_error(p.err, abort_flag, kDevTimeoutFull);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t b_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
-          const uint32_t a_addr = b_addr + Cfg::SLAB_BYTES;
+        for (int kb = kb0; kb < kb1 && ok; ++kb) {
+          for (int sub = 0; sub < NS; ++sub) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+              record_error(p.err, abort_flag, kDevTimeoutFull);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t b_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
+            const uint32_t a_addr = b_addr + Cfg::SUB_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t a_desc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
-#pragma unroll
-            for (int sub = 0; sub < NS; ++sub) {
-              const uint32_t sb = b_addr + sub * Cfg::SUB_BYTES;
-              const uint64_t slab_desc = B_KMAJOR ? make_sdesc_sw128(sb + ks * 32, 16, 1024)
-                                                  : make_sdesc_sw128(sb + ks * 2048, 8192, 1024);
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t a_desc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
+              const uint64_t slab_desc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
+                                                  : make_sdesc_sw128(b_addr + ks * 2048, 8192, 1024);
               mma_f16(d_tmem + sub * MN, slab_desc, a_desc, Cfg::IDESC, (kb != kb0 || ks != 0) ? 1u : 0u);
             }
-          }
-          mma_commit(&empty_bar[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+            mma_commit(&empty_bar[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
         }
         if (ok) mma_commit(&acc_full[acc]);
@@ -363,8 +361,8 @@ cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorM
   p.kbt = int((g.K + 63) / 64);
   p.units = 1LL * g.batch * p.n_tiles * p.kbt;
   const long long grid = p.units < dev.num_sms ? p.units : dev.num_sms;
-  p.ws = reinterpret_cast<float*>(ws);
-  p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + skinny_partials_bytes(dev, NS, MN));
+  p.counters = reinterpret_cast<int*>(ws);
+  p.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes);
   p.err = dev_err;
   kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(tB, tA, p);
   return cudaGetLastError();
@@ -374,6 +372,9 @@ template <int FMT, bool B_KMAJOR, int MN>
 cudaError_t launch_sk_ns(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
                          const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
   switch (skinny_ns(g, dev)) {
+    case 8:
+      if constexpr (MN <= 32) return launch_sk_impl<FMT, B_KMAJOR, MN, 8>(g, tB, tA, ws, dev, dev_err, s);
+      return cudaErrorInvalidValue;
     case 4: return launch_sk_impl<FMT, B_KMAJOR, MN, 4>(g, tB, tA, ws, dev, dev_err, s);
     case 2: return launch_sk_impl<FMT, B_KMAJOR, MN, 2>(g, tB, tA, ws, dev, dev_err, s);
     default: return launch_sk_impl<FMT, B_KMAJOR, MN, 1>(g, tB, tA, ws, dev, dev_err, s);
@@ -394,19 +395,21 @@ cudaError_t launch_sk_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap
 
 int skinny_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-// Sub-slabs per work unit: the widest of 4 / 2 / 1 that leaves every CTA at
-// least four units and pads N by at most 1/8.  CMPX_SKINNY_NS=1|2|4 overrides
-// (tuning experiments).
+// Sub-slabs per work unit: the widest of 8 / 4 / 2 / 1 that fits TMEM
+// (2 buffers x NS x MN columns <= 512), leaves every CTA at least four units,
+// and pads N by at most 1/8.  CMPX_SKINNY_NS=1|2|4|8 overrides (tuning).
 int skinny_ns(const Gemm& g, const DeviceInfo& dev) {
+  const int mn = skinny_mn(g.M);
   static int forced = -1;
   if (forced < 0) {
     const char* e = std::getenv("CMPX_SKINNY_NS");
     forced = 0;
-    if (e != nullptr && (e[0] == '1' || e[0] == '2' || e[0] == '4') && e[1] == 0) forced = e[0] - '0';
+    if (e != nullptr && (e[0] == '1' || e[0] == '2' || e[0] == '4' || e[0] == '8') && e[1] == 0) forced = e[0] - '0';
   }
-  if (forced > 0) return forced;
+  if (forced > 0 && forced * mn <= 256) return forced;
   const int64_t kbt = (g.K + 63) / 64;
-  for (int ns : {4, 2}) {
+  for (int ns : {8, 4, 2}) {
+    if (ns * mn > 256) continue;
     const int64_t w = 128 * ns;
     const int64_t tiles = (g.N + w - 1) / w;
     const int64_t pad = tiles * w - g.N;
@@ -419,11 +422,17 @@ size_t skinny_partials_bytes(const DeviceInfo& dev, int ns, int mn) {
   return size_t(dev.num_sms) * 2 * size_t(ns) * size_t(mn) * 128 * 4;
 }
 
-// fp32 partials for every CTA, then one counter per (tile, epilogue warp).
+int64_t skinny_tiles(const Gemm& g, const DeviceInfo& dev) {
+  const int ns = skinny_ns(g, dev);
+  return g.batch * ((g.N + 128 * ns - 1) / (128 * ns));
+}
+
+// A fixed-size counter region (one int per tile and epilogue warp, for up to
+// kSkinnyMaxTiles tiles) at offset 0, then the fp32 partials.  Every call
+// leaves the counters it used at zero; keeping the region at a fixed place
+// means partials of one call never land on counters of another.
 size_t skinny_workspace_bytes(const Gemm& g, const DeviceInfo& dev) {
-  const int ns = skinny_ns(g, dev), mn = skinny_mn(g.M);
-  const size_t tiles = size_t(g.batch) * size_t((g.N + 128 * ns - 1) / (128 * ns));
-  return skinny_partials_bytes(dev, ns, mn) + ((tiles * 4 * sizeof(int) + 255) / 256) * 256;
+  return kSkinnyCounterBytes + skinny_partials_bytes(dev, skinny_ns(g, dev), skinny_mn(g.M));
 }
 
 cudaError_t launch_skinny(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,

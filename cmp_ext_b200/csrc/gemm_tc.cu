@@ -54,8 +54,16 @@ struct TcCfg {
   static constexpr int CW = 128 / E;         // N-major chunk width in elements
   static constexpr int CHUNK_BYTES = BK * 128;
   static constexpr int KSTEP_BYTES_MN = (32 / E) * 128;  // UMMA_K rows of an MN-major tile
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+  // TMEM accumulator buffers.  fp16/bf16: two (epilogue of tile i overlaps
+  // the main loop of tile i+1), one per tile.  3xTF32: the tensor core's fp32
+  // accumulation over long MMA chains drifts (its rounding is biased), so the
+  // K loop is cut into chunks of KCH k-blocks, each summed afresh in TMEM and
+  // added into fp32 registers by the epilogue with IEEE round-to-nearest;
+  // four buffers let the MMA run three chunks ahead.
+  static constexpr int NACC = FMT == 2 ? 4 : 2;
+  static constexpr int KCH = FMT == 2 ? 4 : (1 << 30);
+  static constexpr uint32_t TMEM_COLS = NACC * BN;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 512;
   static constexpr uint32_t IDESC = make_idesc(FMT == 2 ? 2u : uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, BM, BN);
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert(B_KMAJOR || BN % CW == 0, "BN must be whole N-major chunks");
@@ -166,9 +174,9 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * Cfg::STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* acc_full = empty_bar + STAGES;   // [2]
-  uint64_t* acc_empty = acc_full + 2;        // [2]
-  uint64_t* drain_bar = acc_empty + 2;       // [1]
+  uint64_t* acc_full = empty_bar + STAGES;      // [NACC]
+  uint64_t* acc_empty = acc_full + Cfg::NACC;   // [NACC]
+  uint64_t* drain_bar = acc_empty + Cfg::NACC;  // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -180,7 +188,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < Cfg::NACC; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 128);
     }
@@ -265,54 +273,54 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      int lt = 0;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
-        const int acc = lt & 1;
-        const uint32_t acc_phase = (lt >> 1) & 1;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag)) {
-          record_error(p.err, abort_flag, kDevTimeoutAccEmpty);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
-            record_error(p.err, abort_flag, kDevTimeoutFull);
+      uint32_t cc = 0;  // accumulator chunks issued by this CTA
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        for (int kc = 0; kc < num_kb && ok; kc += Cfg::KCH, ++cc) {
+          const int acc = int(cc % Cfg::NACC);
+          const uint32_t acc_phase = (cc / Cfg::NACC) & 1;
+          if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag)) {
+            record_error(p.err, abort_flag, kDevTimeoutAccEmpty);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + Cfg::NOPS * Cfg::A_BYTES;
+          const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+          const int kend = min(num_kb, kc + Cfg::KCH);
+          for (int kb = kc; kb < kend; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+              record_error(p.err, abort_flag, kDevTimeoutFull);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
+            const uint32_t b_addr = a_addr + Cfg::NOPS * Cfg::A_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t adesc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
-            const uint64_t bdesc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
-                                            : make_sdesc_sw128(b_addr + ks * Cfg::KSTEP_BYTES_MN,
-                                                               Cfg::CHUNK_BYTES, 1024);
-            const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
-            if constexpr (FMT == 2) {
-              const uint64_t adesc_lo = make_sdesc_sw128(a_addr + Cfg::A_BYTES + ks * 32, 16, 1024);
-              const uint64_t bdesc_lo =
-                  B_KMAJOR ? make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * 32, 16, 1024)
-                           : make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * Cfg::KSTEP_BYTES_MN, Cfg::CHUNK_BYTES,
-                                              1024);
-              // small cross terms first, then the dominant hi*hi product
-              mma_tf32(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
-              mma_tf32(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
-              mma_tf32(d_tmem, adesc, bdesc, Cfg::IDESC, 1u);
-            } else {
-              mma_f16(d_tmem, adesc, bdesc, Cfg::IDESC, accum);
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t adesc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
+              const uint64_t bdesc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
+                                              : make_sdesc_sw128(b_addr + ks * Cfg::KSTEP_BYTES_MN,
+                                                                 Cfg::CHUNK_BYTES, 1024);
+              const uint32_t accum = (kb != kc || ks != 0) ? 1u : 0u;
+              if constexpr (FMT == 2) {
+                const uint64_t adesc_lo = make_sdesc_sw128(a_addr + Cfg::A_BYTES + ks * 32, 16, 1024);
+                const uint64_t bdesc_lo = make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * 32, 16, 1024);
+                // small cross terms first, then the dominant hi*hi product
+                mma_tf32(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
+                mma_tf32(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
+                mma_tf32(d_tmem, adesc, bdesc, Cfg::IDESC, 1u);
+              } else {
+                mma_f16(d_tmem, adesc, bdesc, Cfg::IDESC, accum);
+              }
+            }
+            mma_commit(&empty_bar[stage]);  // frees the smem slot once these MMAs retire
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
             }
           }
-          mma_commit(&empty_bar[stage]);  // frees the smem slot once these MMAs retire
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+          if (ok) mma_commit(&acc_full[acc]);  // chunk ready for the epilogue
         }
-        if (ok) mma_commit(&acc_full[acc]);  // accumulator ready for the epilogue
       }
       if (!ok) {
         // Wait for MMAs in flight before TMEM is released.
@@ -326,31 +334,71 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
-    int lt = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
+    uint32_t cc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       int b, tm, tn;
       decode_tile(t, p, b, tm, tn);
-      const int acc = lt & 1;
-      const uint32_t acc_phase = (lt >> 1) & 1;
-      // warp-uniform decision: every lane must take part in tcgen05.ld
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
-      if (!ok) {
-        if (lane == 0) record_error(p.err, abort_flag, kDevTimeoutAccFull);
-        break;
-      }
-      tc_fence_after();
       const int row = tm * Cfg::BM + q * 32 + lane;
       OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
-      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+      if constexpr (FMT == 2) {
+        // Sum the tile's chunks in registers (IEEE fp32 adds), then store.
+        float racc[BN];
+#pragma unroll
+        for (int i = 0; i < BN; ++i) racc[i] = 0.0f;
+        for (int kc = 0; kc < num_kb; kc += Cfg::KCH, ++cc) {
+          const int acc = int(cc % Cfg::NACC);
+          const uint32_t acc_phase = (cc / Cfg::NACC) & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
+          if (!ok) {
+            if (lane == 0) record_error(p.err, abort_flag, kDevTimeoutAccFull);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) racc[c * 32 + i] = __fadd_rn(racc[c * 32 + i], __uint_as_float(r[i]));
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[acc]);
+        }
+        if (!ok) break;
+        if (row < p.M) {
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(racc[c * 32 + i]);
+            store_row32<OutT>(crow, bias, tn * BN + c * 32, p.N, r);
+          }
+        }
+      } else {
+        const int acc = int(cc % Cfg::NACC);
+        const uint32_t acc_phase = (cc / Cfg::NACC) & 1;
+        ++cc;
+        // warp-uniform decision: every lane must take part in tcgen05.ld
+        ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
+        if (!ok) {
+          if (lane == 0) record_error(p.err, abort_flag, kDevTimeoutAccFull);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        if (row < p.M) store_row32<OutT>(crow, bias, tn * BN + c * 32, p.N, r);
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          if (row < p.M) store_row32<OutT>(crow, bias, tn * BN + c * 32, p.N, r);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
     }
   }
 

@@ -56,10 +56,13 @@ cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batc
 // tBop maps B as the MMA's 128-row operand, tAop maps A as the MMA's
 // narrow operand (box rows = mn).  ws: fp32 partials, counters: per-tile ints
 // that are zero on entry and left zero on exit.
+constexpr int64_t kSkinnyMaxTiles = 16384;
+constexpr size_t kSkinnyCounterBytes = size_t(kSkinnyMaxTiles) * 4 * sizeof(int);
 size_t skinny_workspace_bytes(const Gemm& g, const DeviceInfo& dev);
 size_t skinny_partials_bytes(const DeviceInfo& dev, int ns, int mn);
 int skinny_mn(int64_t M);
 int skinny_ns(const Gemm& g, const DeviceInfo& dev);
+int64_t skinny_tiles(const Gemm& g, const DeviceInfo& dev);
 cudaError_t launch_skinny(const Gemm& g, const CUtensorMap& tBop, const CUtensorMap& tAop, void* ws,
                           const DeviceInfo& dev, int* dev_err, cudaStream_t s);
 

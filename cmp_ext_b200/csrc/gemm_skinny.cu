@@ -395,9 +395,11 @@ cudaError_t launch_sk_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap
 
 int skinny_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-// Sub-slabs per work unit: the widest of 8 / 4 / 2 / 1 that fits TMEM
-// (2 buffers x NS x MN columns <= 512), leaves every CTA at least four units,
-// and pads N by at most 1/8.  CMPX_SKINNY_NS=1|2|4|8 overrides (tuning).
+// Sub-slabs per work unit: 2 when that leaves every CTA at least four units
+// and pads N by at most 1/8, else 1.  Measured on config 4 (16 x 28672 x
+// 8192 fp16, B200): 1 -> 68%, 2 -> 79%, 4 -> 72%, 8 -> 58% of HBM copy
+// bandwidth, so wider units are not chosen automatically.
+// CMPX_SKINNY_NS=1|2|4|8 overrides (tuning experiments).
 int skinny_ns(const Gemm& g, const DeviceInfo& dev) {
   const int mn = skinny_mn(g.M);
   static int forced = -1;
@@ -408,7 +410,7 @@ int skinny_ns(const Gemm& g, const DeviceInfo& dev) {
   }
   if (forced > 0 && forced * mn <= 256) return forced;
   const int64_t kbt = (g.K + 63) / 64;
-  for (int ns : {8, 4, 2}) {
+  for (int ns : {2}) {
     if (ns * mn > 256) continue;
     const int64_t w = 128 * ns;
     const int64_t tiles = (g.N + w - 1) / w;

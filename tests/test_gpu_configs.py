@@ -90,8 +90,9 @@ def test_config4_decode_deterministic(cuda):
 
 
 def test_fp32_config5_paths_agree(cuda):
-    """Config 5 on the 3xTF32 tensor-core path and the CUDA-core path: both
-    well inside the fp32 bound, on a row sample."""
+    """Config 5 (1024-row slice) on the 3xTF32 tensor-core path and the
+    CUDA-core path: both inside the fp32 contract (the reference kernel's
+    own error at this K is about 3.7e-6, so the bound is ~1.37e-5)."""
     cfg = CONFIGS[5]
     A, B = make_inputs(cfg, "cuda", seed=3, m=1024)
     rows = _sample_rows(1024, 64)
@@ -100,4 +101,6 @@ def test_fp32_config5_paths_agree(cuda):
         C = _run(A, B, path=path)
         err = o.normwise_err(C[rows].double().cpu().numpy(), C64)
         print(f"config5 path {path}: err {err:.3e}")
-        assert err < 5e-6
+        assert err < 1.3e-5
+        if path == cabi.PATH_TC:
+            assert err < 3e-6  # 3xTF32 with chunked accumulation

@@ -338,6 +338,20 @@ int* device_error_word() {
   return device_state(&d) == CMPX_OK ? d->err_word : nullptr;
 }
 
+int device_facts(DeviceInfo* info, int** err_word) {
+  DeviceState* d = nullptr;
+  const int st = device_state(&d);
+  if (st != CMPX_OK) return st;
+  *info = d->info;
+  *err_word = d->err_word;
+  return CMPX_OK;
+}
+
+int encode_tmap_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
+                   uint64_t ld, uint64_t bstride, uint32_t box_inner, uint32_t box_rows) {
+  return encode_3d(m, dtype, base, inner, rows, batch, ld, bstride, box_inner, box_rows);
+}
+
 }  // namespace cmpx
 
 using namespace cmpx;
@@ -409,6 +423,7 @@ const char* cmpx_status_string(int status) {
     case CMPX_ERR_NO_MEMORY: return "out of device memory for workspace";
     case CMPX_ERR_DEVICE: return "device-side error (bounded wait expired)";
     case CMPX_ERR_WORKSPACE: return "workspace too small";
+    case CMPX_ERR_TOO_LARGE: return "problem larger than the fixed scratch of cmpx_matmul_skinny_noalloc";
     default: return "unknown status";
   }
 }

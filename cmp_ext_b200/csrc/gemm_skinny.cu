@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdlib>
+#include <mutex>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -447,3 +448,118 @@ cudaError_t launch_skinny(const Gemm& g, const CUtensorMap& tB, const CUtensorMa
 }
 
 }  // namespace cmpx
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (see cmpx_matmul_skinny_noalloc in cmpx.h).
+//
+// The scratch lives in a fixed device array of this library: counters first
+// (the same fixed region layout as the library-managed workspace), then fp32
+// partials for up to kNoAllocMaxSms CTAs, two slots each, one 128-column
+// slab of up to 64 accumulator columns.
+namespace cmpx {
+namespace {
+
+constexpr int kNoAllocMaxSms = 160;
+constexpr size_t kNoAllocScratchBytes = kSkinnyCounterBytes + size_t(kNoAllocMaxSms) * 2 * 1 * 64 * 128 * 4;
+
+// In host code this name is only a stand-in for the symbol: its device
+// address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up on
+// the first call per device, with that device current).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CMPX_ERR_CUDA;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return CMPX_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return CMPX_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return CMPX_OK;
+}
+
+template <int FMT, bool B_KMAJOR>
+cudaError_t launch_noalloc_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap& tA, void* ws,
+                              const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  switch (skinny_mn(g.M)) {
+    case 16: return launch_sk_impl<FMT, B_KMAJOR, 16, 1>(g, tB, tA, ws, dev, dev_err, s);
+    case 32: return launch_sk_impl<FMT, B_KMAJOR, 32, 1>(g, tB, tA, ws, dev, dev_err, s);
+    default: return launch_sk_impl<FMT, B_KMAJOR, 64, 1>(g, tB, tA, ws, dev, dev_err, s);
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace cmpx
+
+extern "C" CMPX_API int cmpx_matmul_skinny_noalloc(int dtype, const void* A, const void* B, void* C,
+                                                   const void* bias, int64_t M, int64_t N, int64_t K, int b_layout,
+                                                   cmpx_stream_t stream) {
+  using namespace cmpx;
+  if (dtype != CMPX_F16 && dtype != CMPX_BF16) return CMPX_ERR_INVALID_ARG;
+  if (b_layout != CMPX_B_KN && b_layout != CMPX_B_NK) return CMPX_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return CMPX_ERR_INVALID_ARG;
+  const int64_t tiles = (N + 127) / 128;
+  if (M > 64 || tiles > kSkinnyMaxTiles || K > (int64_t(1) << 31) - 1) return CMPX_ERR_TOO_LARGE;
+  if (M == 0 || N == 0) return CMPX_OK;
+  if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return CMPX_ERR_INVALID_ARG;
+  if (K == 0) return CMPX_ERR_UNSUPPORTED;  // nothing to reduce; use cmpx_gemm
+  if (!al16(A) || !al16(B) || !al16(C) || (K * 2) % 16 != 0 || (N * 2) % 16 != 0) return CMPX_ERR_UNSUPPORTED;
+
+  DeviceInfo dev{};
+  int* err_word = nullptr;
+  int st = device_facts(&dev, &err_word);
+  if (st != CMPX_OK) return st;
+  if (dev.num_sms > kNoAllocMaxSms) return CMPX_ERR_TOO_LARGE;
+  void* ws = nullptr;
+  if ((st = noalloc_scratch(&ws)) != CMPX_OK) return st;
+
+  Gemm g{};
+  g.dtype = dtype;
+  g.A = A;
+  g.B = B;
+  g.C = C;
+  g.bias = bias;
+  g.batch = 1;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.lda = K;
+  g.ldb = b_layout == CMPX_B_KN ? N : K;
+  g.ldc = N;
+  g.sa = M * K;
+  g.sb = N * K;
+  g.sc = M * N;
+  g.b_kmajor = b_layout == CMPX_B_NK ? 1 : 0;
+
+  CUtensorMap tB, tA;
+  st = g.b_kmajor ? encode_tmap_3d(&tB, dtype, B, K, N, 1, K, g.sb, 64, 128)
+                  : encode_tmap_3d(&tB, dtype, B, N, K, 1, N, g.sb, 64, 64);
+  if (st != CMPX_OK) return st;
+  st = encode_tmap_3d(&tA, dtype, A, K, M, 1, K, g.sa, 64, uint32_t(skinny_mn(M)));
+  if (st != CMPX_OK) return st;
+
+  // Counters must start at zero; a call that was cut short could have left
+  // some behind, so clear the ones this call uses.
+  if (cudaMemsetAsync(ws, 0, size_t(tiles) * 4 * sizeof(int), stream) != cudaSuccess) return CMPX_ERR_CUDA;
+  cudaError_t e;
+  if (dtype == CMPX_F16)
+    e = g.b_kmajor ? launch_noalloc_mn<0, true>(g, tB, tA, ws, dev, err_word, stream)
+                   : launch_noalloc_mn<0, false>(g, tB, tA, ws, dev, err_word, stream);
+  else
+    e = g.b_kmajor ? launch_noalloc_mn<1, true>(g, tB, tA, ws, dev, err_word, stream)
+                   : launch_noalloc_mn<1, false>(g, tB, tA, ws, dev, err_word, stream);
+  return e == cudaSuccess ? CMPX_OK : CMPX_ERR_CUDA;
+}

@@ -79,4 +79,11 @@ cudaError_t launch_add_bias(int dtype, void* C, const void* bias, int64_t rows, 
 // Device error word (see ptx.cuh DeviceError).
 int* device_error_word();
 
+// Facts and error word of the current device (initialising them once), and
+// the TMA descriptor encoder the dispatcher uses; for entry points that live
+// next to their kernels.
+int device_facts(DeviceInfo* info, int** err_word);
+int encode_tmap_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
+                   uint64_t ld, uint64_t bstride, uint32_t box_inner, uint32_t box_rows);
+
 }  // namespace cmpx

@@ -56,7 +56,8 @@ typedef enum {
   CMPX_ERR_CUDA = 3,        /* a CUDA runtime/driver call or kernel launch failed */
   CMPX_ERR_NO_MEMORY = 4,   /* library-managed workspace could not be allocated */
   CMPX_ERR_DEVICE = 5,      /* a kernel reported a device-side error (bounded wait expired) */
-  CMPX_ERR_WORKSPACE = 6    /* caller workspace smaller than cmpx_gemm_workspace_size() */
+  CMPX_ERR_WORKSPACE = 6,   /* caller workspace smaller than cmpx_gemm_workspace_size() */
+  CMPX_ERR_TOO_LARGE = 7    /* problem exceeds the fixed scratch of cmpx_matmul_skinny_noalloc() */
 } cmpx_status;
 
 typedef enum { CMPX_F16 = 0, CMPX_BF16 = 1, CMPX_F32 = 2 } cmpx_dtype;
@@ -125,6 +126,37 @@ CMPX_API int cmpx_gemm_select_path(const cmpx_gemm_args* args);
  * the reference it is correct for odd (fp16) and non-multiple-of-4 (fp32)
  * column counts. */
 CMPX_API int cmpx_add_bias(int dtype, void* C, const void* bias, int64_t rows, int64_t cols, cmpx_stream_t stream);
+
+/* Skinny-M (decode) matmul that allocates no device memory.  No counterpart
+ * in the reference, which allocates nothing itself because it has no
+ * scratch at all.
+ *
+ * For callers that cannot call cudaMalloc: code that runs inside a fixed
+ * memory budget handed out by a host framework, allocator hooks that must not
+ * recurse into the allocator, or a process that sets the device up once and
+ * may not allocate afterwards.  cmpx_gemm's skinny path needs ~2.7-20 MB of
+ * scratch (fp32 partial sums of the split K range, plus per-tile counters)
+ * and gets it from cudaMalloc or from a caller workspace; this variant uses
+ * a fixed array compiled into libcmpx.so instead (about 10.8 MB, held on
+ * every GPU that loads the library until the process exits).
+ *
+ * Computes C[M,N] = A[M,K] * B (+ bias[N]) for fp16/bf16 with packed
+ * row-major operands: A [M,K]; B [K,N] (b_layout CMPX_B_KN) or [N,K]
+ * (CMPX_B_NK); C [M,N]; same kernel and fp32 accumulation as cmpx_gemm's
+ * skinny path, with one 128-column slab per work unit.  Limits: M <= 64,
+ * ceil(N/128) <= 16384, at most 160 SMs on the device -- otherwise
+ * CMPX_ERR_TOO_LARGE.  Pointers and row strides must be 16-byte aligned
+ * (else CMPX_ERR_UNSUPPORTED).
+ *
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  Every call on a device shares the one array:
+ * calls that may overlap on the GPU (different streams, or different host
+ * threads) race and must be serialised by the caller.  The per-tile counters
+ * the kernel needs at zero are cleared (cudaMemsetAsync) on `stream` at the
+ * start of every call. */
+CMPX_API int cmpx_matmul_skinny_noalloc(int dtype, const void* A, const void* B, void* C, const void* bias,
+                                        int64_t M, int64_t N, int64_t K, int b_layout, cmpx_stream_t stream);
 
 /* Reads and clears the device-side error word of the current device
  * (synchronises the device).  *code receives the first error a kernel

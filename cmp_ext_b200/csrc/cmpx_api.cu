@@ -225,6 +225,29 @@ int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
   return sk_ok ? CMPX_PATH_SKINNY : CMPX_PATH_TC;
 }
 
+// fp16/bf16 tile kernel choice: CTA pairs (0 = single-CTA 128x256 tiles,
+// else the pair tile's N: 256 when 256x256 pair tiles still fill at least
+// eight waves of SM pairs, otherwise 128).  M <= 128 keeps the single-CTA
+// kernel (a 256-row pair tile would be half empty).  CMPX_TC_PAIR=0|128|256
+// overrides (tuning experiments).
+int tc_pair_n(const Gemm& g, const DeviceInfo& dev) {
+  static int forced = -2;
+  if (forced == -2) {
+    const char* e = std::getenv("CMPX_TC_PAIR");
+    forced = -1;
+    if (e != nullptr) {
+      if (!std::strcmp(e, "0")) forced = 0;
+      else if (!std::strcmp(e, "128")) forced = 128;
+      else if (!std::strcmp(e, "256")) forced = 256;
+    }
+  }
+  if (forced >= 0) return forced;
+  if (g.M <= 128) return 0;
+  const int64_t pairs = dev.num_sms / 2;
+  const int64_t tiles256 = g.batch * ((g.M + 255) / 256) * ((g.N + 255) / 256);
+  return tiles256 >= 8 * pairs ? 256 : 128;
+}
+
 size_t f32_split_bytes(const Gemm& g) {
   const size_t a = size_t(g.batch) * size_t(g.M) * size_t(g.K);
   const size_t b = size_t(g.batch) * size_t(g.K) * size_t(g.N);
@@ -279,6 +302,13 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
     CUtensorMap tA, tB;
     st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.batch, g.lda, g.sa, 64, 128);
     if (st != CMPX_OK) return st;
+    const int pair_n = tc_pair_n(g, d->info);
+    if (pair_n > 0) {
+      st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, uint32_t(pair_n / 2))
+                      : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
+      if (st != CMPX_OK) return st;
+      return cuda_status(launch_tc2_f16(g, tA, tB, pair_n, d->info, d->err_word, s));
+    }
     st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 256)
                     : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
     if (st != CMPX_OK) return st;

@@ -1,0 +1,368 @@
+// Persistent tcgen05 GEMM on CTA pairs (cta_group::2) for fp16 / bf16.
+//
+// Same product and arithmetic as gemm_tc.cu (fp32 accumulation in TMEM,
+// one rounding to the output type; replaces the reference's SIMT kernels
+// src/cuda/fp16_matmul.cu:63-283 and src/cuda/bf16_matmul.cu:51-226), with
+// the output tile computed by two SMs together:
+//   * a cluster of two CTAs owns a 256 x PN tile; CTA rank r holds rows
+//     [128 r, 128 r + 128) of the A tile and columns [PN/2 r, PN/2 (r+1)) of
+//     the B tile in its shared memory;
+//   * the leader (rank 0) issues one tcgen05.mma.cta_group::2 (M = 256,
+//     N = PN, K = 16) per k-step, which reads both CTAs' shared memory and
+//     writes each CTA's 128 accumulator rows into that CTA's TMEM;
+//   * both CTAs load their own halves with TMA; the loads complete on the
+//     leader's "full" barrier (no multicast: every byte lands in the CTA that
+//     loaded it), and the leader's MMA completion is multicast to both CTAs'
+//     "empty" and "accumulator full" barriers;
+//   * each CTA's epilogue warps drain their own TMEM rows and report back to
+//     the leader's "accumulator empty" barrier.
+// Per SM this halves the B operand traffic of a 128 x PN tile, and the
+// 256 x 128 pair tile gives twice as many tiles as a 128 x 256 tile for the
+// same work per SM, which cuts the wave-quantisation tail on mid-size
+// problems.
+//
+// Warp roles per CTA (192 threads): warp 0 TMA producer, warp 1 TMEM
+// allocation (both CTAs) and MMA issue (leader only), warps 2..5 epilogue.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace cmpx {
+namespace {
+
+struct Tc2Params {
+  void* C;
+  const void* bias;
+  int M, N, K, batch;
+  long long ldc, stride_c;
+  int tiles_m, tiles_n, group_m;  // in pair tiles (256 x PN)
+  int* err;
+};
+
+template <int FMT, bool B_KMAJOR, int PN, int STAGES_>
+struct Tc2Cfg {
+  static constexpr int BK = 64;                  // 128 bytes of K
+  static constexpr int BH = PN / 2;              // B columns held by one CTA
+  static constexpr int STAGES = STAGES_;
+  static constexpr int A_BYTES = 128 * 128;      // 128 rows x 64 K x 2 B
+  static constexpr int B_BYTES = BH * 128;       // BH columns x 64 K x 2 B
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int NACC = 512 / PN;          // TMEM accumulators per CTA
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 512;
+  static constexpr uint32_t IDESC = make_idesc(uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, 256, PN);
+  static_assert(BH % 64 == 0, "B half must be whole 64-column chunks");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+};
+
+__device__ __forceinline__ void decode_tile2(int t, const Tc2Params& p, int& b, int& tm, int& tn) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  b = t / per_batch;
+  const int r = t - b * per_batch;
+  const int gw = p.group_m * p.tiles_n;
+  const int g = r / gw;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.tiles_m - first_m, p.group_m);
+  const int rr = r - g * gw;
+  tm = first_m + rr % gm;
+  tn = rr / gm;
+}
+
+__device__ __forceinline__ void record_error2(int* err, volatile int* abort, int code) {
+  *abort = 1;
+  atomicCAS(err, 0, code);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32_2(T v);
+template <>
+__device__ __forceinline__ float to_f32_2<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32_2<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+__device__ __forceinline__ uint32_t pack2_2(float a, float b, __half*) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2_2(float a, float b, __nv_bfloat16*) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 32 consecutive accumulator columns of one output row -> +bias -> 16-bit
+// output; full 16-byte groups inside [0, N) use vector stores.
+template <typename T>
+__device__ __forceinline__ void store_row32_16(T* crow, const T* bias, int col0, int N, const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < N) v[i] += to_f32_2<T>(bias[col0 + i]);
+  }
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int c = col0 + g * 8;
+    if (c + 8 <= N) {
+      uint4 q;
+      q.x = pack2_2(v[g * 8 + 0], v[g * 8 + 1], (T*)nullptr);
+      q.y = pack2_2(v[g * 8 + 2], v[g * 8 + 3], (T*)nullptr);
+      q.z = pack2_2(v[g * 8 + 4], v[g * 8 + 5], (T*)nullptr);
+      q.w = pack2_2(v[g * 8 + 6], v[g * 8 + 7], (T*)nullptr);
+      *reinterpret_cast<uint4*>(crow + c) = q;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (c + i < N) {
+          if constexpr (std::is_same<T, __half>::value)
+            crow[c + i] = __float2half_rn(v[g * 8 + i]);
+          else
+            crow[c + i] = __float2bfloat16_rn(v[g * 8 + i]);
+        }
+    }
+  }
+}
+
+template <int FMT, bool B_KMAJOR, int PN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const Tc2Params p) {
+  using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES>;
+  using OutT = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;
+  uint64_t* acc_empty = acc_full + Cfg::NACC;
+  uint64_t* drain_bar = acc_empty + Cfg::NACC;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);   // used in the leader only
+      mbar_init(&empty_bar[s], 1);  // leader's MMA commit, multicast to both CTAs
+    }
+    for (int a = 0; a < Cfg::NACC; ++a) {
+      mbar_init(&acc_full[a], 1);     // leader's MMA commit, multicast to both CTAs
+      mbar_init(&acc_empty[a], 256);  // used in the leader only: both CTAs' epilogue threads
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_holder, Cfg::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int total_tiles = p.tiles_m * p.tiles_n * p.batch;
+  const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+        int b, tm, tn;
+        decode_tile2(t, p, b, tm, tn);
+        const int m0 = tm * 256 + int(rank) * 128;
+        const int n0 = tn * PN + int(rank) * Cfg::BH;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
+            record_error2(p.err, abort_flag, kDevTimeoutEmpty);
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_cluster(&full_bar[stage], 0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+          uint8_t* sA = smem + size_t(stage) * Cfg::STAGE_BYTES;
+          uint8_t* sB = sA + Cfg::A_BYTES;
+          const int k0 = kb * Cfg::BK;
+          tma_load_3d_pair(sA, &tmA, full_leader, k0, m0, b);
+          if (B_KMAJOR) {
+            tma_load_3d_pair(sB, &tmB, full_leader, k0, n0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < Cfg::BH / 64; ++j) tma_load_3d_pair(sB + j * 8192, &tmB, full_leader, n0 + 64 * j, k0, b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Give copies already issued time to land before the CTA exits.
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      uint32_t lt = 0;
+      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters, ++lt) {
+        const int acc = int(lt % Cfg::NACC);
+        const uint32_t acc_phase = (lt / Cfg::NACC) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag)) {
+          record_error2(p.err, abort_flag, kDevTimeoutAccEmpty);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * PN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+            record_error2(p.err, abort_flag, kDevTimeoutFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t adesc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
+            const uint64_t bdesc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
+                                            : make_sdesc_sw128(b_addr + ks * 2048, 8192, 1024);
+            mma_f16_pair(d_tmem, adesc, bdesc, Cfg::IDESC, (kb | ks) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair_mc(&empty_bar[stage], 0x3);  // both CTAs' slots are free once these retire
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mma_commit_pair_mc(&acc_full[acc], 0x3);
+      }
+      if (!ok) {
+        mma_commit_pair_mc(drain_bar, 0x1);
+        volatile int never = 0;
+        mbar_wait(drain_bar, 0, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    OutT* C = reinterpret_cast<OutT*>(p.C);
+    const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
+    uint32_t lt = 0;
+    for (int t = cluster_id; t < total_tiles; t += num_clusters, ++lt) {
+      int b, tm, tn;
+      decode_tile2(t, p, b, tm, tn);
+      const int acc = int(lt % Cfg::NACC);
+      const uint32_t acc_phase = (lt / Cfg::NACC) & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
+      if (!ok) {
+        if (lane == 0) record_error2(p.err, abort_flag, kDevTimeoutAccFull);
+        break;
+      }
+      tc_fence_after();
+      const int row = tm * 256 + int(rank) * 128 + q * 32 + lane;
+      OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PN);
+#pragma unroll 1
+      for (int c = 0; c < PN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + c * 32, p.N, r);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_cluster(&acc_empty[acc], 0));
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int FMT, bool B_KMAJOR, int PN, int STAGES>
+cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, const DeviceInfo& dev,
+                            int* dev_err, cudaStream_t s) {
+  using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES>;
+  auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES>;
+  static_assert(Cfg::SMEM <= 232448, "shared memory budget");
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM));
+  if (e != cudaSuccess) return e;
+  Tc2Params p;
+  p.C = g.C;
+  p.bias = g.bias;
+  p.M = int(g.M);
+  p.N = int(g.N);
+  p.K = int(g.K);
+  p.batch = int(g.batch);
+  p.ldc = g.ldc;
+  p.stride_c = g.sc;
+  p.tiles_m = int((g.M + 255) / 256);
+  p.tiles_n = int((g.N + PN - 1) / PN);
+  p.group_m = 8;
+  p.err = dev_err;
+  const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
+  const long long pairs = dev.num_sms / 2;
+  const long long clusters = total < pairs ? total : pairs;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(2 * clusters), 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tA, tB, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Pair-tile width: 256 x 128 (twice the tiles, for fewer-wave problems) by
+// default; the B half held per CTA is pair_n / 2 columns.
+cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n,
+                           const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  if (pair_n == 256) {
+    if (g.dtype == CMPX_F16)
+      return g.b_kmajor ? launch_tc2_impl<0, true, 256, 6>(g, tA, tB, dev, dev_err, s)
+                        : launch_tc2_impl<0, false, 256, 6>(g, tA, tB, dev, dev_err, s);
+    return g.b_kmajor ? launch_tc2_impl<1, true, 256, 6>(g, tA, tB, dev, dev_err, s)
+                      : launch_tc2_impl<1, false, 256, 6>(g, tA, tB, dev, dev_err, s);
+  }
+  if (g.dtype == CMPX_F16)
+    return g.b_kmajor ? launch_tc2_impl<0, true, 128, 8>(g, tA, tB, dev, dev_err, s)
+                      : launch_tc2_impl<0, false, 128, 8>(g, tA, tB, dev, dev_err, s);
+  return g.b_kmajor ? launch_tc2_impl<1, true, 128, 8>(g, tA, tB, dev, dev_err, s)
+                    : launch_tc2_impl<1, false, 128, 8>(g, tA, tB, dev, dev_err, s);
+}
+
+}  // namespace cmpx

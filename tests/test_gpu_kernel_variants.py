@@ -1,0 +1,22 @@
+"""The tile-kernel parity tests again, under each fp16/bf16 tile-kernel
+variant the dispatcher can pick: single-CTA 128x256 tiles, and CTA-pair
+(cta_group::2) 256x128 and 256x256 tiles.  The variant is fixed per process
+(CMPX_TC_PAIR), so each runs in a child pytest."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.mark.parametrize("pair", ["0", "128", "256"])
+def test_tile_kernel_variant(cuda, pair):
+    env = dict(os.environ, CMPX_TC_PAIR=pair)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.join(HERE, "test_gpu_parity.py"), "-k", "tc_path or batched or bias"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

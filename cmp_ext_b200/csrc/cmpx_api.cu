@@ -225,11 +225,13 @@ int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
   return sk_ok ? CMPX_PATH_SKINNY : CMPX_PATH_TC;
 }
 
-// fp16/bf16 tile kernel choice: CTA pairs (0 = single-CTA 128x256 tiles,
-// else the pair tile's N: 256 when 256x256 pair tiles still fill at least
-// eight waves of SM pairs, otherwise 128).  M <= 128 keeps the single-CTA
-// kernel (a 256-row pair tile would be half empty).  CMPX_TC_PAIR=0|128|256
-// overrides (tuning experiments).
+// fp16/bf16 tile kernel choice: 0 = single-CTA 128x256 tiles, else CTA
+// pairs with 256 x pair_n tiles.  Measured on a B200 (bench.py): 256x256
+// pair tiles beat both alternatives on every config tried (config 3:
+// 0.91 vs 0.89 single-CTA vs 0.64 for 256x128 pairs; config 2, 4096^3:
+// 0.84 vs 0.77 vs 0.55), so pairs with pair_n = 256 are used whenever
+// M > 128 (below that a 256-row pair tile would be at least half empty).
+// CMPX_TC_PAIR=0|128|256 overrides (tuning experiments and tests).
 int tc_pair_n(const Gemm& g, const DeviceInfo& dev) {
   static int forced = -2;
   if (forced == -2) {
@@ -242,10 +244,7 @@ int tc_pair_n(const Gemm& g, const DeviceInfo& dev) {
     }
   }
   if (forced >= 0) return forced;
-  if (g.M <= 128) return 0;
-  const int64_t pairs = dev.num_sms / 2;
-  const int64_t tiles256 = g.batch * ((g.M + 255) / 256) * ((g.N + 255) / 256);
-  return tiles256 >= 8 * pairs ? 256 : 128;
+  return g.M <= 128 ? 0 : 256;
 }
 
 size_t f32_split_bytes(const Gemm& g) {

@@ -1,5 +1,5 @@
 """The tile-kernel parity tests again, under each fp16/bf16 tile-kernel
-variant the dispatcher can pick: single-CTA 128x256 tiles, and CTA-pair
+variant the dispatcher can pick: single-CTA 128x256 tiles (chosen for M <= 128), and CTA-pair
 (cta_group::2) 256x128 and 256x256 tiles.  The variant is fixed per process
 (CMPX_TC_PAIR), so each runs in a child pytest."""
 import os

@@ -257,6 +257,10 @@ size_t f32_split_bytes(const Gemm& g) {
 size_t workspace_for(const Gemm& g, int path, const DeviceInfo& dev) {
   if (path == CMPX_PATH_SKINNY) return skinny_workspace_bytes(g, dev);
   if (path == CMPX_PATH_TC && g.dtype == CMPX_F32) return f32_split_bytes(g);
+  if (path == CMPX_PATH_TC) {
+    const int pair_n = tc_pair_n(g, dev);
+    return pair_n > 0 ? tc2_workspace_bytes(g, pair_n, dev) : 0;
+  }
   return 0;
 }
 
@@ -281,7 +285,9 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
       if (!aligned16(args->workspace)) return CMPX_ERR_INVALID_ARG;
       ws = args->workspace;
     } else {
-      st = library_workspace(*d, path == CMPX_PATH_SKINNY ? 1 : 0, need, &ws);
+      // slot 1 keeps its counter region zero between calls (skinny and
+      // CTA-pair stream-K); slot 0 is plain scratch (3xTF32 splits)
+      st = library_workspace(*d, g.dtype == CMPX_F32 ? 0 : 1, need, &ws);
       if (st != CMPX_OK) return st;
     }
   }
@@ -306,7 +312,7 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
       st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, uint32_t(pair_n / 2))
                       : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
       if (st != CMPX_OK) return st;
-      return cuda_status(launch_tc2_f16(g, tA, tB, pair_n, d->info, d->err_word, s));
+      return cuda_status(launch_tc2_f16(g, tA, tB, pair_n, ws, d->info, d->err_word, s));
     }
     st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 256)
                     : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);

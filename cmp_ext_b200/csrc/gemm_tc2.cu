@@ -38,8 +38,51 @@ struct Tc2Params {
   int M, N, K, batch;
   long long ldc, stride_c;
   int tiles_m, tiles_n, group_m;  // in pair tiles (256 x PN)
+  // Data-parallel + stream-K split: tiles [0, dp_tiles) are computed whole,
+  // round-robin over the pairs; the k-blocks of the remaining sk_tiles tiles
+  // (sk_units = sk_tiles * k-blocks) are split evenly over all pairs.
+  int dp_tiles, sk_tiles;
+  long long sk_units;
+  float* ws;      // [pair][slot 2][rank 2][128][PN] fp32 partials of split tiles
+  int* counters;  // [sk tile][rank 2][epilogue warp 4], zero on entry and exit
   int* err;
 };
+
+// One unit of work of a pair: output tile `tile`, k-blocks [kb0, kb1).
+// skt >= 0 marks a stream-K tile (its index among the split tiles).
+struct WorkItem {
+  int tile, kb0, kb1, skt;
+};
+
+__device__ __forceinline__ long long sk_begin(long long g, long long U, long long P) { return g * U / P; }
+__device__ __forceinline__ long long sk_owner(long long u, long long U, long long P) { return ((u + 1) * P - 1) / U; }
+
+// The item-th work item of pair `c` (false when there is none): first its
+// whole data-parallel tiles, then the pieces of its stream-K unit range cut
+// at tile boundaries.  Every role of both CTAs walks the same sequence.
+__device__ __forceinline__ bool work_item(const Tc2Params& p, int c, int P, int num_kb, int item, WorkItem& w) {
+  const int n_dp = c < p.dp_tiles ? (p.dp_tiles - c + P - 1) / P : 0;
+  if (item < n_dp) {
+    w.tile = c + item * P;
+    w.kb0 = 0;
+    w.kb1 = num_kb;
+    w.skt = -1;
+    return true;
+  }
+  if (p.sk_tiles == 0) return false;
+  const long long U = p.sk_units;
+  const long long u0 = sk_begin(c, U, P), u1 = sk_begin(c + 1, U, P);
+  const int j = item - n_dp;
+  const long long s = j == 0 ? u0 : (u0 / num_kb + j) * (long long)num_kb;
+  if (s >= u1) return false;
+  const long long t = s / num_kb;
+  const long long e = min(u1, (t + 1) * (long long)num_kb);
+  w.skt = int(t);
+  w.tile = p.dp_tiles + int(t);
+  w.kb0 = int(s - t * num_kb);
+  w.kb1 = int(e - t * num_kb);
+  return true;
+}
 
 template <int FMT, bool B_KMAJOR, int PN, int STAGES_>
 struct Tc2Cfg {
@@ -168,7 +211,6 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  const int total_tiles = p.tiles_m * p.tiles_n * p.batch;
   const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
@@ -180,12 +222,13 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tmap(&tmB);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+      WorkItem w;
+      for (int item = 0; ok && work_item(p, cluster_id, num_clusters, num_kb, item, w); ++item) {
         int b, tm, tn;
-        decode_tile2(t, p, b, tm, tn);
+        decode_tile2(w.tile, p, b, tm, tn);
         const int m0 = tm * 256 + int(rank) * 128;
         const int n0 = tn * PN + int(rank) * Cfg::BH;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
             record_error2(p.err, abort_flag, kDevTimeoutEmpty);
             ok = false;
@@ -222,7 +265,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       uint32_t lt = 0;
-      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters, ++lt) {
+      WorkItem w;
+      for (int item = 0; ok && work_item(p, cluster_id, num_clusters, num_kb, item, w); ++item, ++lt) {
         const int acc = int(lt % Cfg::NACC);
         const uint32_t acc_phase = (lt / Cfg::NACC) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag)) {
@@ -232,7 +276,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * PN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
             record_error2(p.err, abort_flag, kDevTimeoutFull);
             ok = false;
@@ -246,7 +290,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t adesc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
             const uint64_t bdesc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
                                             : make_sdesc_sw128(b_addr + ks * 2048, 8192, 1024);
-            mma_f16_pair(d_tmem, adesc, bdesc, Cfg::IDESC, (kb | ks) != 0 ? 1u : 0u);
+            mma_f16_pair(d_tmem, adesc, bdesc, Cfg::IDESC, (kb != w.kb0 || ks != 0) ? 1u : 0u);
           }
           mma_commit_pair_mc(&empty_bar[stage], 0x3);  // both CTAs' slots are free once these retire
           if (++stage == STAGES) {
@@ -268,9 +312,12 @@ __global__ void __launch_bounds__(192, 1)
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
     uint32_t lt = 0;
-    for (int t = cluster_id; t < total_tiles; t += num_clusters, ++lt) {
+    const long long P = num_clusters;
+    const long long first_skt = p.sk_tiles > 0 ? sk_begin(cluster_id, p.sk_units, P) / num_kb : -1;
+    WorkItem w;
+    for (int item = 0; work_item(p, cluster_id, num_clusters, num_kb, item, w); ++item, ++lt) {
       int b, tm, tn;
-      decode_tile2(t, p, b, tm, tn);
+      decode_tile2(w.tile, p, b, tm, tn);
       const int acc = int(lt % Cfg::NACC);
       const uint32_t acc_phase = (lt / Cfg::NACC) & 1;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
@@ -279,18 +326,78 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      const int row = tm * 256 + int(rank) * 128 + q * 32 + lane;
+      const int lrow = q * 32 + lane;  // row within this CTA's 128-row half
+      const int row = tm * 256 + int(rank) * 128 + lrow;
       OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PN);
+      long long g_lo = 0, g_hi = 0;
+      if (w.skt >= 0) {
+        const long long t_u0 = (long long)w.skt * num_kb;
+        g_lo = sk_owner(t_u0, p.sk_units, P);
+        g_hi = sk_owner(t_u0 + num_kb - 1, p.sk_units, P);
+      }
+      const bool whole = w.skt < 0 || g_lo == g_hi;
+      float* part = nullptr;
+      if (!whole) {
+        const int slot = (w.skt == first_skt) ? 0 : 1;
+        part = p.ws + ((size_t(cluster_id) * 2 + slot) * 2 + rank) * 128 * PN + size_t(lrow) * PN;
+      }
 #pragma unroll 1
       for (int c = 0; c < PN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
-        if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + c * 32, p.N, r);
+        if (whole) {
+          if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + c * 32, p.N, r);
+        } else {
+          float4* dst = reinterpret_cast<float4*>(part + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            __stcg(dst + i, make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                        __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])));
+        }
       }
       tc_fence_before();
       mbar_arrive_cluster(mapa_cluster(&acc_empty[acc], 0));
+
+      if (!whole) {
+        // The last part of this split tile to arrive (per CTA half and
+        // epilogue warp) sums the parts in pair order, adds the bias, rounds
+        // once and stores; it then zeroes the counter for the next launch.
+        __threadfence();
+        __syncwarp();
+        int prev = 0;
+        int* ctr = p.counters + (size_t(w.skt) * 2 + rank) * 4 + q;
+        if (lane == 0) prev = atomicAdd(ctr, 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == int(g_hi - g_lo)) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < PN / 32; ++c) {
+            float sum[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sum[i] = 0.0f;
+            for (long long gg = g_lo; gg <= g_hi; ++gg) {
+              const int sl = (w.skt == sk_begin(gg, p.sk_units, P) / num_kb) ? 0 : 1;
+              const float4* src = reinterpret_cast<const float4*>(
+                  p.ws + ((size_t(gg) * 2 + sl) * 2 + rank) * 128 * PN + size_t(lrow) * PN + c * 32);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 v = __ldcg(src + i);
+                sum[4 * i] += v.x;
+                sum[4 * i + 1] += v.y;
+                sum[4 * i + 2] += v.z;
+                sum[4 * i + 3] += v.w;
+              }
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(sum[i]);
+            if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + c * 32, p.N, r);
+          }
+          if (lane == 0) *ctr = 0;
+        }
+      }
     }
   }
 
@@ -304,8 +411,8 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int FMT, bool B_KMAJOR, int PN, int STAGES>
-cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, const DeviceInfo& dev,
-                            int* dev_err, cudaStream_t s) {
+cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
+                            const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
   using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES>;
   auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
@@ -326,7 +433,14 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const long long pairs = dev.num_sms / 2;
-  const long long clusters = total < pairs ? total : pairs;
+  const int num_kb = int((g.K + Cfg::BK - 1) / Cfg::BK);
+  const long long rem = ws != nullptr ? total % pairs : 0;  // tiles of the last, partial wave
+  p.dp_tiles = int(total - rem);
+  p.sk_tiles = int(rem);
+  p.sk_units = rem * num_kb;
+  p.counters = reinterpret_cast<int*>(ws);
+  p.ws = ws != nullptr ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes) : nullptr;
+  const long long clusters = rem > 0 ? pairs : (total < pairs ? total : pairs);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(2 * clusters), 1, 1);
@@ -349,20 +463,29 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
 
 // Pair-tile width: 256 x 128 (twice the tiles, for fewer-wave problems) by
 // default; the B half held per CTA is pair_n / 2 columns.
-cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n,
+// Workspace for the stream-K part (0 when the tiles fill whole waves): the
+// shared fixed counter region, then [pair][2 slots][2 ranks][128][pair_n] fp32.
+size_t tc2_workspace_bytes(const Gemm& g, int pair_n, const DeviceInfo& dev) {
+  const long long pairs = dev.num_sms / 2;
+  const long long total = g.batch * ((g.M + 255) / 256) * ((g.N + pair_n - 1) / pair_n);
+  if (total % pairs == 0) return 0;
+  return kSkinnyCounterBytes + size_t(pairs) * 2 * 2 * 128 * size_t(pair_n) * 4;
+}
+
+cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n, void* ws,
                            const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
   if (pair_n == 256) {
     if (g.dtype == CMPX_F16)
-      return g.b_kmajor ? launch_tc2_impl<0, true, 256, 6>(g, tA, tB, dev, dev_err, s)
-                        : launch_tc2_impl<0, false, 256, 6>(g, tA, tB, dev, dev_err, s);
-    return g.b_kmajor ? launch_tc2_impl<1, true, 256, 6>(g, tA, tB, dev, dev_err, s)
-                      : launch_tc2_impl<1, false, 256, 6>(g, tA, tB, dev, dev_err, s);
+      return g.b_kmajor ? launch_tc2_impl<0, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s)
+                        : launch_tc2_impl<0, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s);
+    return g.b_kmajor ? launch_tc2_impl<1, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s)
+                      : launch_tc2_impl<1, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s);
   }
   if (g.dtype == CMPX_F16)
-    return g.b_kmajor ? launch_tc2_impl<0, true, 128, 8>(g, tA, tB, dev, dev_err, s)
-                      : launch_tc2_impl<0, false, 128, 8>(g, tA, tB, dev, dev_err, s);
-  return g.b_kmajor ? launch_tc2_impl<1, true, 128, 8>(g, tA, tB, dev, dev_err, s)
-                    : launch_tc2_impl<1, false, 128, 8>(g, tA, tB, dev, dev_err, s);
+    return g.b_kmajor ? launch_tc2_impl<0, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s)
+                      : launch_tc2_impl<0, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s);
+  return g.b_kmajor ? launch_tc2_impl<1, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s)
+                    : launch_tc2_impl<1, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s);
 }
 
 }  // namespace cmpx

@@ -44,7 +44,11 @@ cudaError_t launch_tc_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMa
 // CTA-pair (cta_group::2) variant of the fp16/bf16 tile kernel: 256 x pair_n
 // output tiles (pair_n = 128 or 256).  tA box = {64, 128}; tB box = {64, 64}
 // for a [K,N] B, {64, pair_n / 2} for an [N,K] B.
-cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n,
+// ws: stream-K workspace of tc2_workspace_bytes() (shares the skinny
+// path's layout: fixed zeroed counter region first), or nullptr to run
+// whole tiles only.
+size_t tc2_workspace_bytes(const Gemm& g, int pair_n, const DeviceInfo& dev);
+cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n, void* ws,
                            const DeviceInfo& dev, int* dev_err, cudaStream_t s);
 
 // 3xTF32 tensor-core kernel for fp32: tA/tA2 map the tf32 hi/lo splits of A,

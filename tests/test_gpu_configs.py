@@ -67,17 +67,24 @@ def test_config_within_reference_error(cuda, cid, nrows):
 
 
 @pytest.mark.parametrize("cid", [3, 5])
-def test_m_sharded_equals_full(cuda, cid):
+def test_m_sharded_matches_full(cuda, cid):
     """Config 3/5 are M-sharded over up to 8 GPUs: shard products (rows
-    r0:r1, B replicated) concatenated must equal the full product exactly."""
+    r0:r1, B replicated) concatenated must match the full product.  The split
+    of the last wave's k-range (stream-K) depends on the tile count, so fp32
+    partial sums may be added in a different order: the bound is one unit in
+    the last place of the output type at max|C|.  Repeated identical calls
+    are bit-identical."""
     from cmp_ext_b200.distributed import shard_rows
 
     cfg = CONFIGS[cid]
     A, B = make_inputs(cfg, "cuda", seed=1)
     full = _run(A, B)
+    assert torch.equal(full, _run(A, B)), "repeated calls must be deterministic"
+    ulp = 2.0 ** -7 if cfg.dtype == torch.bfloat16 else 2.0 ** -23
     for world in (2, 8):
-        parts = [_run(A, B, rows=shard_rows(cfg.M, world, r)) for r in range(world)]
-        assert torch.equal(torch.cat(parts), full), f"world {world}"
+        parts = torch.cat([_run(A, B, rows=shard_rows(cfg.M, world, r)) for r in range(world)])
+        err = o.normwise_err(parts.double().cpu().numpy(), full.double().cpu().numpy())
+        assert err <= ulp, f"world {world}: {err}"
 
 
 def test_config4_decode_deterministic(cuda):

@@ -42,6 +42,7 @@ struct Tc2Params {
   // round-robin over the pairs; the k-blocks of the remaining sk_tiles tiles
   // (sk_units = sk_tiles * k-blocks) are split evenly over all pairs.
   int dp_tiles, sk_tiles;
+  int sk_pairs;  // pairs sharing the stream-K units: min(pairs, sk_units), so none is empty
   long long sk_units;
   float* ws;      // [pair][slot 2][rank 2][128][PN] fp32 partials of split tiles
   int* counters;  // [sk tile][rank 2][epilogue warp 4], zero on entry and exit
@@ -69,9 +70,9 @@ __device__ __forceinline__ bool work_item(const Tc2Params& p, int c, int P, int 
     w.skt = -1;
     return true;
   }
-  if (p.sk_tiles == 0) return false;
+  if (p.sk_tiles == 0 || c >= p.sk_pairs) return false;
   const long long U = p.sk_units;
-  const long long u0 = sk_begin(c, U, P), u1 = sk_begin(c + 1, U, P);
+  const long long u0 = sk_begin(c, U, p.sk_pairs), u1 = sk_begin(c + 1, U, p.sk_pairs);
   const int j = item - n_dp;
   const long long s = j == 0 ? u0 : (u0 / num_kb + j) * (long long)num_kb;
   if (s >= u1) return false;
@@ -312,8 +313,9 @@ __global__ void __launch_bounds__(192, 1)
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
     uint32_t lt = 0;
-    const long long P = num_clusters;
-    const long long first_skt = p.sk_tiles > 0 ? sk_begin(cluster_id, p.sk_units, P) / num_kb : -1;
+    const long long P = p.sk_pairs;
+    const long long first_skt =
+        (p.sk_tiles > 0 && cluster_id < p.sk_pairs) ? sk_begin(cluster_id, p.sk_units, P) / num_kb : -1;
     WorkItem w;
     for (int item = 0; work_item(p, cluster_id, num_clusters, num_kb, item, w); ++item, ++lt) {
       int b, tm, tn;
@@ -372,28 +374,35 @@ __global__ void __launch_bounds__(192, 1)
         prev = __shfl_sync(0xffffffffu, prev, 0);
         if (prev == int(g_hi - g_lo)) {
           __threadfence();
+          // Two halves of the row; per half and part, all 16 float4 loads are
+          // issued before any is used (memory-level parallelism).
 #pragma unroll 1
-          for (int c = 0; c < PN / 32; ++c) {
-            float sum[32];
+          for (int h = 0; h < PN / 128; ++h) {
+            float sum[128];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) sum[i] = 0.0f;
+            for (int i = 0; i < 128; ++i) sum[i] = 0.0f;
             for (long long gg = g_lo; gg <= g_hi; ++gg) {
               const int sl = (w.skt == sk_begin(gg, p.sk_units, P) / num_kb) ? 0 : 1;
               const float4* src = reinterpret_cast<const float4*>(
-                  p.ws + ((size_t(gg) * 2 + sl) * 2 + rank) * 128 * PN + size_t(lrow) * PN + c * 32);
+                  p.ws + ((size_t(gg) * 2 + sl) * 2 + rank) * 128 * PN + size_t(lrow) * PN + h * 128);
+              float4 v[32];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 v = __ldcg(src + i);
-                sum[4 * i] += v.x;
-                sum[4 * i + 1] += v.y;
-                sum[4 * i + 2] += v.z;
-                sum[4 * i + 3] += v.w;
+              for (int i = 0; i < 32; ++i) v[i] = __ldcg(src + i);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                sum[4 * i] += v[i].x;
+                sum[4 * i + 1] += v[i].y;
+                sum[4 * i + 2] += v[i].z;
+                sum[4 * i + 3] += v[i].w;
               }
             }
-            uint32_t r[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(sum[i]);
-            if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + c * 32, p.N, r);
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(sum[c * 32 + i]);
+              if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + h * 128 + c * 32, p.N, r);
+            }
           }
           if (lane == 0) *ctr = 0;
         }
@@ -434,13 +443,19 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const long long pairs = dev.num_sms / 2;
   const int num_kb = int((g.K + Cfg::BK - 1) / Cfg::BK);
-  const long long rem = ws != nullptr ? total % pairs : 0;  // tiles of the last, partial wave
-  p.dp_tiles = int(total - rem);
-  p.sk_tiles = int(rem);
-  p.sk_units = rem * num_kb;
+  // Stream-K region: the last, partial wave plus one full wave before it (so
+  // each split tile has only two or three parts), or everything when there
+  // is less than a wave.
+  const long long rem = total % pairs;
+  long long sk = 0;
+  if (ws != nullptr && rem != 0) sk = total >= pairs ? rem + pairs : total;
+  p.dp_tiles = int(total - sk);
+  p.sk_tiles = int(sk);
+  p.sk_units = sk * num_kb;
+  p.sk_pairs = int(p.sk_units < pairs ? p.sk_units : pairs);
   p.counters = reinterpret_cast<int*>(ws);
   p.ws = ws != nullptr ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes) : nullptr;
-  const long long clusters = rem > 0 ? pairs : (total < pairs ? total : pairs);
+  const long long clusters = sk > 0 ? pairs : (total < pairs ? total : pairs);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(2 * clusters), 1, 1);

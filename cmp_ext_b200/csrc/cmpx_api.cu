@@ -247,6 +247,18 @@ int tc_pair_n(const Gemm& g, const DeviceInfo& dev) {
   return g.M <= 128 ? 0 : 256;
 }
 
+// Whether the CTA-pair kernel splits its last wave stream-K (needs the
+// workspace).  CMPX_TC_STREAMK=0|1 overrides (tuning experiments).
+bool tc_streamk(const Gemm& g) {
+  (void)g;
+  static int forced = -1;
+  if (forced < 0) {
+    const char* e = std::getenv("CMPX_TC_STREAMK");
+    forced = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return forced == 1;
+}
+
 size_t f32_split_bytes(const Gemm& g) {
   const size_t a = size_t(g.batch) * size_t(g.M) * size_t(g.K);
   const size_t b = size_t(g.batch) * size_t(g.K) * size_t(g.N);
@@ -259,7 +271,7 @@ size_t workspace_for(const Gemm& g, int path, const DeviceInfo& dev) {
   if (path == CMPX_PATH_TC && g.dtype == CMPX_F32) return f32_split_bytes(g);
   if (path == CMPX_PATH_TC) {
     const int pair_n = tc_pair_n(g, dev);
-    return pair_n > 0 ? tc2_workspace_bytes(g, pair_n, dev) : 0;
+    return (pair_n > 0 && tc_streamk(g)) ? tc2_workspace_bytes(g, pair_n, dev) : 0;
   }
   return 0;
 }

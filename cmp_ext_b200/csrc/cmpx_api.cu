@@ -248,13 +248,17 @@ int tc_pair_n(const Gemm& g, const DeviceInfo& dev) {
 }
 
 // Whether the CTA-pair kernel splits its last wave stream-K (needs the
-// workspace).  CMPX_TC_STREAMK=0|1 overrides (tuning experiments).
+// workspace).  Off by default: A/B on a B200 (bench.py, same session) put it
+// behind whole tiles at every size tried -- 4096^3 fp16: 0.71 vs 0.82;
+// bf16 2048x8192x8192: 0.72-0.79 vs 0.86; 4096x8192x8192: 0.70-0.85 vs
+// 0.76-0.85 -- the partial-sum round trip through L2 costs more than the
+// partial-wave tail it removes.  CMPX_TC_STREAMK=1 turns it on.
 bool tc_streamk(const Gemm& g) {
   (void)g;
   static int forced = -1;
   if (forced < 0) {
     const char* e = std::getenv("CMPX_TC_STREAMK");
-    forced = (e != nullptr && e[0] == '0') ? 0 : 1;
+    forced = (e != nullptr && e[0] == '1') ? 1 : 0;
   }
   return forced == 1;
 }

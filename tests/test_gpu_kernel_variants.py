@@ -1,7 +1,8 @@
 """The tile-kernel parity tests again, under each fp16/bf16 tile-kernel
 variant the dispatcher can pick: single-CTA 128x256 tiles (chosen for M <= 128), and CTA-pair
-(cta_group::2) 256x128 and 256x256 tiles.  The variant is fixed per process
-(CMPX_TC_PAIR), so each runs in a child pytest."""
+(cta_group::2) 256x128 and 256x256 tiles, each CTA-pair size also with the
+opt-in stream-K split of the last wave.  The variant is fixed per process
+(CMPX_TC_PAIR, CMPX_TC_STREAMK), so each runs in a child pytest."""
 import os
 import subprocess
 import sys
@@ -13,9 +14,9 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.mark.parametrize("pair", ["0", "128", "256"])
-def test_tile_kernel_variant(cuda, pair):
-    env = dict(os.environ, CMPX_TC_PAIR=pair)
+@pytest.mark.parametrize("pair,streamk", [("0", "0"), ("128", "0"), ("256", "0"), ("256", "1"), ("128", "1")])
+def test_tile_kernel_variant(cuda, pair, streamk):
+    env = dict(os.environ, CMPX_TC_PAIR=pair, CMPX_TC_STREAMK=streamk)
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
                         os.path.join(HERE, "test_gpu_parity.py"), "-k", "tc_path or batched or bias"],
                        env=env, capture_output=True, text=True, timeout=900)

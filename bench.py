@@ -155,7 +155,9 @@ def op_for(dtype):
 def kernel_name(cfg) -> str:
     if cfg.dtype == torch.float32:
         return "gemm_tc_kernel(3xTF32)"
-    return "gemm_skinny_kernel" if cfg.M <= 64 else "gemm_tc_kernel"
+    if cfg.M <= 64:
+        return "gemm_skinny_kernel"
+    return "gemm_tc2_kernel (CTA pairs, 256x256)" if cfg.M > 128 else "gemm_tc_kernel"
 
 
 # ------------------------------------------------------------------ CPU legs

@@ -5,6 +5,9 @@ reference's pybind module, src/main.cpp:1594-1602, plus the 2-D forms):
 
     linear(input, weight, bias=None)   y = input @ weight.T + bias
     bmm(input, mat2)                   (B,M,K) x (B,K,N) -> (B,M,N)
+    conv2d(input, weight, bias=None, stride=1, padding=0, dilation=1, groups=1)
+                                       the 1x1 / stride 1 / padding 0 case, as one
+                                       batched GEMM on NCHW (no layout copies)
     fp16_matmul(a, b) / bf16_matmul(a, b) / fp32_matmul(a, b)
                                        a[M,K] @ b[K,N] -> [M,N]
 
@@ -21,7 +24,7 @@ import torch  # noqa: F401  (loads libtorch / c10 before the shim)
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcmpx.so")
 
-_OPS = ("linear", "bmm", "fp16_matmul", "bf16_matmul", "fp32_matmul", "_set_path", "version")
+_OPS = ("linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul", "_set_path", "version")
 
 
 def _load_ext():
@@ -47,4 +50,4 @@ def __getattr__(name):
     raise AttributeError(f"module 'cmp_ext_b200' has no attribute {name!r}")
 
 
-__all__ = ["linear", "bmm", "fp16_matmul", "bf16_matmul", "fp32_matmul", "LIB_PATH", "version"]
+__all__ = ["linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul", "LIB_PATH", "version"]

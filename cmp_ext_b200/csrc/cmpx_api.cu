@@ -180,6 +180,8 @@ Gemm to_gemm(const cmpx_gemm_args* a) {
   g.sb = a->batch > 1 ? a->stride_b : (a->b_layout == CMPX_B_KN ? a->K * a->ldb : a->N * a->ldb);
   g.sc = a->batch > 1 ? a->stride_c : a->M * a->ldc;
   g.b_kmajor = a->b_layout == CMPX_B_NK ? 1 : 0;
+  g.a_bcast = (a->batch > 1 && a->stride_a == 0) ? 1 : 0;
+  g.bias_m = a->bias_along_m ? 1 : 0;
   return g;
 }
 
@@ -314,14 +316,14 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
     st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 128)
                     : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
     if (st != CMPX_OK) return st;
-    st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.batch, g.lda, g.sa, 64, mn);
+    st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.a_bcast ? 1 : g.batch, g.lda, g.sa, 64, mn);
     if (st != CMPX_OK) return st;
     return cuda_status(launch_skinny(g, tB, tA, ws, d->info, d->err_word, s));
   }
 
   if (g.dtype != CMPX_F32) {
     CUtensorMap tA, tB;
-    st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.batch, g.lda, g.sa, 64, 128);
+    st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.a_bcast ? 1 : g.batch, g.lda, g.sa, 64, 128);
     if (st != CMPX_OK) return st;
     const int pair_n = tc_pair_n(g, d->info);
     if (pair_n > 0) {
@@ -347,7 +349,8 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   float* a_lo = reinterpret_cast<float*>(base + up(a_elems));
   float* b_hi = reinterpret_cast<float*>(base + 2 * up(a_elems));
   float* b_lo = reinterpret_cast<float*>(base + 2 * up(a_elems) + up(b_elems));
-  cudaError_t e = launch_split_tf32(reinterpret_cast<const float*>(g.A), a_hi, a_lo, g.batch, g.M, g.K, g.lda, g.sa,
+  const int64_t a_batch = g.a_bcast ? 1 : g.batch;  // a shared A is split once
+  cudaError_t e = launch_split_tf32(reinterpret_cast<const float*>(g.A), a_hi, a_lo, a_batch, g.M, g.K, g.lda, g.sa,
                                     false, s);
   if (e != cudaSuccess) return CMPX_ERR_CUDA;
   const int64_t b_rows = g.b_kmajor ? g.N : g.K, b_cols = g.b_kmajor ? g.K : g.N;
@@ -356,8 +359,8 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   if (e != cudaSuccess) return CMPX_ERR_CUDA;
   CUtensorMap tA, tA2, tB, tB2;
   const uint64_t sa = uint64_t(g.M) * uint64_t(g.K), sb = uint64_t(g.N) * uint64_t(g.K);
-  if ((st = encode_3d(&tA, CMPX_F32, a_hi, g.K, g.M, g.batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
-  if ((st = encode_3d(&tA2, CMPX_F32, a_lo, g.K, g.M, g.batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
+  if ((st = encode_3d(&tA, CMPX_F32, a_hi, g.K, g.M, a_batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
+  if ((st = encode_3d(&tA2, CMPX_F32, a_lo, g.K, g.M, a_batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
   if ((st = encode_3d(&tB, CMPX_F32, b_hi, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
   if ((st = encode_3d(&tB2, CMPX_F32, b_lo, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
   return cuda_status(launch_tc_tf32x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));

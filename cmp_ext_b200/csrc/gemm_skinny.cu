@@ -40,6 +40,8 @@ struct SkParams {
   long long units;  // batch * n_tiles * kbt
   float* ws;      // [grid][2][MN][128] fp32 partials
   int* counters;  // [batch * n_tiles][4] (one per epilogue warp quadrant)
+  int a_bcast;
+  int bias_m;
   int* err;
 };
 
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(192, 1)
             tma_load_3d(sB, &tmB, &full_bar[stage], n0 + sub * 128, k0, b);
             tma_load_3d(sB + 8192, &tmB, &full_bar[stage], n0 + sub * 128 + 64, k0, b);
           }
-          tma_load_3d(sA, &tmA, &full_bar[stage], k0, 0, b);
+          tma_load_3d(sA, &tmA, &full_bar[stage], k0, 0, p.a_bcast ? 0 : b);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -280,10 +282,13 @@ __global__ void __launch_bounds__(192, 1)
         if (whole) {
           // column n of C^T is C[:, n]: lanes write consecutive n (coalesced)
           if (n < p.N) {
-            const float bv = bias != nullptr ? to_f32<T>(bias[n]) : 0.0f;
+            const float bv = (bias != nullptr && !p.bias_m) ? to_f32<T>(bias[n]) : 0.0f;
 #pragma unroll
             for (int j = 0; j < MN; ++j)
-              if (j < p.M) from_f32(v[j] + bv, cb + size_t(j) * p.ldc + n);
+              if (j < p.M) {
+                const float rb = (bias != nullptr && p.bias_m) ? to_f32<T>(bias[j]) : 0.0f;
+                from_f32(v[j] + bv + rb, cb + size_t(j) * p.ldc + n);
+              }
           }
         } else {
           float* part = p.ws + (((size_t(blockIdx.x) * 2 + slot) * NS + sub) * MN) * 128;
@@ -320,10 +325,13 @@ __global__ void __launch_bounds__(192, 1)
             }
             const int n = nt0 + sub * 128;
             if (n < p.N) {
-              const float bv = bias != nullptr ? to_f32<T>(bias[n]) : 0.0f;
+              const float bv = (bias != nullptr && !p.bias_m) ? to_f32<T>(bias[n]) : 0.0f;
 #pragma unroll
               for (int j = 0; j < MN; ++j)
-                if (j < p.M) from_f32(acc_s[j] + bv, cb + size_t(j) * p.ldc + n);
+                if (j < p.M) {
+                  const float rb = (bias != nullptr && p.bias_m) ? to_f32<T>(bias[j]) : 0.0f;
+                  from_f32(acc_s[j] + bv + rb, cb + size_t(j) * p.ldc + n);
+                }
             }
           }
           if (lane == 0) p.counters[tile * 4 + q] = 0;
@@ -364,6 +372,8 @@ cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorM
   const long long grid = p.units < dev.num_sms ? p.units : dev.num_sms;
   p.counters = reinterpret_cast<int*>(ws);
   p.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes);
+  p.a_bcast = g.a_bcast;
+  p.bias_m = g.bias_m;
   p.err = dev_err;
   kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(tB, tA, p);
   return cudaGetLastError();

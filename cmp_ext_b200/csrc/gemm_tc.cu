@@ -36,6 +36,8 @@ struct TcParams {
   int M, N, K, batch;
   long long ldc, stride_c;
   int tiles_m, tiles_n, group_m;
+  int a_bcast;
+  int bias_m;
   int* err;
 };
 
@@ -112,10 +114,11 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
 // Full 16-byte groups inside [0, N) use vector stores; a ragged last group
 // falls back to scalar stores.
 template <typename T>
-__device__ __forceinline__ void store_row32(T* crow, const T* bias, int col0, int N, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void store_row32(T* crow, const T* bias, float rowb, int col0, int N,
+                                            const uint32_t (&r)[32]) {
   float v[32];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + rowb;
   if (bias != nullptr) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -231,8 +234,9 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sB = sA + Cfg::NOPS * Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           const int k0 = kb * Cfg::BK;
-          tma_load_3d(sA, &tmA, &full_bar[stage], k0, m0, b);
-          if (FMT == 2) tma_load_3d(sA + Cfg::A_BYTES, &tmA2, &full_bar[stage], k0, m0, b);
+          const int za = p.a_bcast ? 0 : b;
+          tma_load_3d(sA, &tmA, &full_bar[stage], k0, m0, za);
+          if (FMT == 2) tma_load_3d(sA + Cfg::A_BYTES, &tmA2, &full_bar[stage], k0, m0, za);
           if (B_KMAJOR) {
             tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0, b);
             if (FMT == 2) tma_load_3d(sB + Cfg::B_BYTES, &tmB2, &full_bar[stage], k0, n0, b);
@@ -341,6 +345,8 @@ __global__ void __launch_bounds__(192, 1)
       decode_tile(t, p, b, tm, tn);
       const int row = tm * Cfg::BM + q * 32 + lane;
       OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      const OutT* colb = p.bias_m ? nullptr : bias;
+      const float rowb = (p.bias_m && bias != nullptr && row < p.M) ? to_f32<OutT>(bias[row]) : 0.0f;
       if constexpr (FMT == 2) {
         // Sum the tile's chunks in registers (IEEE fp32 adds), then store.
         float racc[BN];
@@ -374,7 +380,7 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t r[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(racc[c * 32 + i]);
-            store_row32<OutT>(crow, bias, tn * BN + c * 32, p.N, r);
+            store_row32<OutT>(crow, colb, rowb, tn * BN + c * 32, p.N, r);
           }
         }
       } else {
@@ -394,7 +400,7 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);
           tmem_ld_wait();
-          if (row < p.M) store_row32<OutT>(crow, bias, tn * BN + c * 32, p.N, r);
+          if (row < p.M) store_row32<OutT>(crow, colb, rowb, tn * BN + c * 32, p.N, r);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
@@ -431,6 +437,8 @@ cudaError_t launch_tc_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   p.tiles_m = int((g.M + Cfg::BM - 1) / Cfg::BM);
   p.tiles_n = int((g.N + BN - 1) / BN);
   p.group_m = 16;
+  p.a_bcast = g.a_bcast;
+  p.bias_m = g.bias_m;
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const int grid = int(total < dev.num_sms ? total : dev.num_sms);

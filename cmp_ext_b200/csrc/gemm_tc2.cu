@@ -46,6 +46,8 @@ struct Tc2Params {
   long long sk_units;
   float* ws;      // [pair][slot 2][rank 2][128][PN] fp32 partials of split tiles
   int* counters;  // [sk tile][rank 2][epilogue warp 4], zero on entry and exit
+  int a_bcast;
+  int bias_m;
   int* err;
 };
 
@@ -138,10 +140,11 @@ __device__ __forceinline__ uint32_t pack2_2(float a, float b, __nv_bfloat16*) {
 // 32 consecutive accumulator columns of one output row -> +bias -> 16-bit
 // output; full 16-byte groups inside [0, N) use vector stores.
 template <typename T>
-__device__ __forceinline__ void store_row32_16(T* crow, const T* bias, int col0, int N, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void store_row32_16(T* crow, const T* bias, float rowb, int col0, int N,
+                                               const uint32_t (&r)[32]) {
   float v[32];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + rowb;
   if (bias != nullptr) {
 #pragma unroll
     for (int i = 0; i < 32; ++i)
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sA = smem + size_t(stage) * Cfg::STAGE_BYTES;
           uint8_t* sB = sA + Cfg::A_BYTES;
           const int k0 = kb * Cfg::BK;
-          tma_load_3d_pair(sA, &tmA, full_leader, k0, m0, b);
+          tma_load_3d_pair(sA, &tmA, full_leader, k0, m0, p.a_bcast ? 0 : b);
           if (B_KMAJOR) {
             tma_load_3d_pair(sB, &tmB, full_leader, k0, n0, b);
           } else {
@@ -331,6 +334,8 @@ __global__ void __launch_bounds__(192, 1)
       const int lrow = q * 32 + lane;  // row within this CTA's 128-row half
       const int row = tm * 256 + int(rank) * 128 + lrow;
       OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      const OutT* colb = p.bias_m ? nullptr : bias;
+      const float rowb = (p.bias_m && bias != nullptr && row < p.M) ? to_f32_2<OutT>(bias[row]) : 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PN);
       long long g_lo = 0, g_hi = 0;
       if (w.skt >= 0) {
@@ -350,7 +355,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
         if (whole) {
-          if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + c * 32, p.N, r);
+          if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r);
         } else {
           float4* dst = reinterpret_cast<float4*>(part + c * 32);
 #pragma unroll
@@ -401,7 +406,7 @@ __global__ void __launch_bounds__(192, 1)
               uint32_t r[32];
 #pragma unroll
               for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(sum[c * 32 + i]);
-              if (row < p.M) store_row32_16<OutT>(crow, bias, tn * PN + h * 128 + c * 32, p.N, r);
+              if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + h * 128 + c * 32, p.N, r);
             }
           }
           if (lane == 0) *ctr = 0;
@@ -439,6 +444,8 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
   p.tiles_m = int((g.M + 255) / 256);
   p.tiles_n = int((g.N + PN - 1) / PN);
   p.group_m = 8;
+  p.a_bcast = g.a_bcast;
+  p.bias_m = g.bias_m;
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const long long pairs = dev.num_sms / 2;

@@ -26,6 +26,8 @@ struct Gemm {
   int64_t lda, ldb, ldc;
   int64_t sa, sb, sc;
   int b_kmajor;
+  int a_bcast;  // batch > 1 and stride_a == 0: every batch entry uses the same A
+  int bias_m;   // bias has M entries (one per row) instead of N (one per column)
 };
 
 inline int elem_bytes(int dtype) { return dtype == CMPX_F32 ? 4 : 2; }

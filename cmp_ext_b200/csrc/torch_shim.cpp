@@ -193,6 +193,86 @@ torch::Tensor matmul_2d(const torch::Tensor& a_in, const torch::Tensor& b_in, at
   return c;
 }
 
+std::vector<int64_t> pair_param(const py::object& o) {
+  if (py::isinstance<py::int_>(o)) {
+    const int64_t v = o.cast<int64_t>();
+    return {v, v};
+  }
+  std::vector<int64_t> v = o.cast<std::vector<int64_t>>();
+  TORCH_CHECK(!v.empty(), "conv2d: empty stride/padding/dilation");
+  if (v.size() == 1) v.push_back(v[0]);
+  return v;
+}
+
+// conv2d with the reference's signature and checks (custom_conv2d_forward,
+// src/main.cpp:363-424; wrapper src/main.cpp:491-505).  This build provides
+// its 1x1 / stride 1 / padding 0 / dilation 1 branch (src/main.cpp:402-424).
+// The reference runs that branch as an NCHW->NHWC copy, linear (with its
+// weight transpose copy) and an NHWC->NCHW copy.  Here it is one batched
+// GEMM per call, with no copies: in NCHW,
+// out[b] (C_out x H*W) = weight (C_out x C_in) . input[b] (C_in x H*W),
+// with the weight shared by every batch entry and the bias fused.
+torch::Tensor conv2d(torch::Tensor input, torch::Tensor weight, c10::optional<torch::Tensor> bias,
+                     py::object stride_arg, py::object padding_arg, py::object dilation_arg, int64_t groups) {
+  const std::vector<int64_t> stride = pair_param(stride_arg);
+  const std::vector<int64_t> padding = pair_param(padding_arg);
+  const std::vector<int64_t> dilation = pair_param(dilation_arg);
+  TORCH_CHECK(input.dim() == 4, "Input must be 4D (NCHW)");
+  TORCH_CHECK(weight.dim() == 4, "Weight must be 4D (O I/G kH kW)");
+  TORCH_CHECK(input.device() == weight.device(), "Device mismatch");
+  TORCH_CHECK(groups == 1, "Currently only groups=1 is supported in this custom op");
+  TORCH_CHECK(input.size(1) == weight.size(1), "Input channels mismatch weight channels");
+  const bool one_by_one = weight.size(2) == 1 && weight.size(3) == 1 && stride[0] == 1 && stride[1] == 1 &&
+                          padding[0] == 0 && padding[1] == 0 && dilation[0] == 1 && dilation[1] == 1;
+  TORCH_CHECK(one_by_one,
+              "cmpext3.conv2d (B200 build) provides the 1x1, stride 1, padding 0, dilation 1 convolution only; "
+              "general convolutions are not part of this build");
+  TORCH_CHECK(input.is_cuda(), "cmpext3.conv2d expects CUDA tensors");
+  TORCH_CHECK(input.scalar_type() == weight.scalar_type(), "Dtype mismatch");
+  const int64_t B = input.size(0), Cin = input.size(1), H = input.size(2), W = input.size(3);
+  const int64_t Cout = weight.size(0), HW = H * W;
+  if (Cout % 2 != 0 && input.scalar_type() == at::kHalf) {
+    TORCH_CHECK(false, "Custom FP16 Kernel requires even Output Channels (N)");
+  }
+  const int dt = dtype_code(input.scalar_type());
+  TORCH_CHECK(dt >= 0, "Unsupported dtype");
+  c10::cuda::CUDAGuard guard(input.device());
+  input = input.contiguous();
+  weight = weight.contiguous();
+  torch::Tensor bias_t;
+  if (bias.has_value() && bias->defined()) {
+    bias_t = *bias;
+    TORCH_CHECK(bias_t.device() == input.device(), "Bias device mismatch");
+    TORCH_CHECK(bias_t.dtype() == input.dtype(), "Bias dtype mismatch");
+    TORCH_CHECK(bias_t.dim() == 1, "Bias must be 1D");
+    TORCH_CHECK(bias_t.size(0) == Cout, "Bias size mismatch");
+    bias_t = bias_t.contiguous();
+  }
+  torch::Tensor output = torch::empty({B, Cout, H, W}, input.options());
+  if (B == 0 || Cout == 0 || HW == 0) return output;
+  // The bias is per output channel = per GEMM row: fused with bias_along_m.
+  cmpx_gemm_args a = base_args(dt);
+  a.A = weight.data_ptr();
+  a.B = input.data_ptr();
+  a.C = output.data_ptr();
+  a.batch = B;
+  a.M = Cout;
+  a.N = HW;
+  a.K = Cin;
+  a.lda = Cin;
+  a.ldb = HW;
+  a.ldc = HW;
+  a.stride_a = 0;
+  a.stride_b = Cin * HW;
+  a.stride_c = Cout * HW;
+  a.b_layout = CMPX_B_KN;
+  a.bias = bias_t.defined() ? bias_t.data_ptr() : nullptr;
+  a.bias_along_m = 1;
+  a.path = g_forced_path;
+  check_status(cmpx_gemm(&a, current_stream()), "cmpext3.conv2d");
+  return output;
+}
+
 torch::Tensor fp16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kHalf, "fp16_matmul"); }
 torch::Tensor bf16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kBFloat16, "bf16_matmul"); }
 torch::Tensor fp32_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kFloat, "fp32_matmul"); }
@@ -203,6 +283,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear", &linear, "y = input @ weight.T + bias (cmpext3.linear)", py::arg("input"), py::arg("weight"),
         py::arg("bias") = py::none());
   m.def("bmm", &bmm, "batched matmul (B,M,K) x (B,K,N) (cmpext3.bmm)", py::arg("input"), py::arg("mat2"));
+  m.def("conv2d", &conv2d, "conv2d (cmpext3.conv2d); the 1x1 / stride 1 / padding 0 / dilation 1 case",
+        py::arg("input"), py::arg("weight"), py::arg("bias") = py::none(), py::arg("stride") = 1,
+        py::arg("padding") = 0, py::arg("dilation") = 1, py::arg("groups") = 1);
   m.def("fp16_matmul", &fp16_matmul, "a[M,K] @ b[K,N] in fp16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
   m.def("bf16_matmul", &bf16_matmul, "a[M,K] @ b[K,N] in bf16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
   m.def("fp32_matmul", &fp32_matmul, "a[M,K] @ b[K,N] in fp32 (3xTF32)", py::arg("a"), py::arg("b"));

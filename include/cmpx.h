@@ -83,11 +83,13 @@ typedef struct {
   const void* bias;       /* optional [N] (NULL = none), fused into the epilogue */
   int64_t batch, M, N, K; /* all >= 0 */
   int64_t lda, ldb, ldc;
-  int64_t stride_a, stride_b, stride_c;
+  int64_t stride_a, stride_b, stride_c;  /* stride_a == 0 with batch > 1: one A shared by every batch entry */
   int b_layout;           /* cmpx_b_layout */
   int path;               /* cmpx_path (AUTO unless a test forces one) */
   void* workspace;        /* optional caller scratch (device); NULL = library-managed */
   size_t workspace_bytes;
+  int bias_along_m;       /* 0: bias[N] added to every row; 1: bias[M] added to every column
+                             (per output channel of a 1x1 convolution in NCHW) */
 } cmpx_gemm_args;
 
 /* Replaces launch_matmul_fp16 (reference src/cuda/fp16_matmul.cu:301-340;

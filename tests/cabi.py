@@ -40,6 +40,7 @@ class GemmArgs(ctypes.Structure):
         ("path", ctypes.c_int),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("bias_along_m", ctypes.c_int),
     ]
 
 

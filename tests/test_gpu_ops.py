@@ -1,0 +1,81 @@
+"""The cmpext3-compatible operators on the GPU: linear (weight read in place,
+fused bias, N-D input), bmm (one batched launch), conv2d's 1x1 case (batched
+GEMM with a shared weight and a per-channel bias), against torch fp32
+references of the same op."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+import cmp_ext_b200 as cx
+import cabi
+from oracle import oracle as o
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 2e-3, torch.bfloat16: 1.6e-2, torch.float32: 1e-4}
+
+
+def _err(got, want):
+    return o.normwise_err(got.double().cpu().numpy(), want.double().cpu().numpy())
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(2, 64, 96, 16, 16), (3, 128, 32, 8, 8), (2, 32, 200, 7, 7), (1, 256, 512, 32, 32)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("bias", [False, True])
+def test_conv2d_1x1(cuda, dtype, shape, bias):
+    B, Cin, Cout, H, W = shape
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(B, Cin, H, W, generator=g, device="cuda").to(dtype)
+    w = (torch.randn(Cout, Cin, 1, 1, generator=g, device="cuda") * 0.1).to(dtype)
+    b = torch.randn(Cout, generator=g, device="cuda").to(dtype) if bias else None
+    y = cx.conv2d(x, w, b)
+    assert y.shape == (B, Cout, H, W) and y.dtype == dtype and y.is_contiguous()
+    want = F.conv2d(x.float().cpu(), w.float().cpu(), b.float().cpu() if bias else None)
+    assert _err(y, want) <= TOL[dtype]
+
+
+def test_conv2d_tuple_params(cuda):
+    x = torch.randn(2, 16, 4, 4, device="cuda", dtype=torch.float16)
+    w = torch.randn(8, 16, 1, 1, device="cuda", dtype=torch.float16)
+    y = cx.conv2d(x, w, None, (1, 1), (0, 0), (1, 1), 1)
+    assert _err(y, F.conv2d(x.float(), w.float())) <= TOL[torch.float16]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_linear_nd_bias(cuda, dtype):
+    g = torch.Generator(device="cuda").manual_seed(8)
+    x = torch.randn(2, 3, 40, 320, generator=g, device="cuda").to(dtype)
+    w = (torch.randn(200, 320, generator=g, device="cuda") * 0.05).to(dtype)
+    b = torch.randn(200, generator=g, device="cuda").to(dtype)
+    y = cx.linear(x, w, b)
+    assert y.shape == (2, 3, 40, 200)
+    assert _err(y, x.float() @ w.float().t() + b.float()) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_bmm(cuda, dtype):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    a = torch.randn(5, 300, 136, generator=g, device="cuda").to(dtype)
+    b = (torch.randn(5, 136, 264, generator=g, device="cuda") * 0.1).to(dtype)
+    c = cx.bmm(a, b)
+    assert c.shape == (5, 300, 264)
+    assert _err(c, torch.bmm(a.float(), b.float())) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("path", [cabi.PATH_TC, cabi.PATH_SKINNY, cabi.PATH_SIMT])
+def test_shared_a_and_row_bias_cabi(cuda, path):
+    """stride_a = 0 (one A for every batch entry) and bias_along_m through the
+    C ABI on each path."""
+    Bt, M, N, K = 3, 48 if path == cabi.PATH_SKINNY else 200, 264, 136
+    g = torch.Generator(device="cuda").manual_seed(10)
+    A = torch.randn(M, K, generator=g, device="cuda").half()
+    Bm = (torch.randn(Bt, K, N, generator=g, device="cuda") * 0.1).half()
+    bias = torch.randn(M, generator=g, device="cuda").half()
+    C = torch.full((Bt, M, N), float("nan"), device="cuda", dtype=torch.float16)
+    args = cabi.gemm_args(A, Bm[0], C[0], bias=bias, batch=Bt, sa=0, sb=K * N, sc=M * N, path=path)
+    args.bias_along_m = 1
+    assert cabi.gemm(args) == cabi.OK
+    torch.cuda.synchronize()
+    want = torch.matmul(A.float(), Bm.float()) + bias.float()[None, :, None]
+    assert _err(C, want) <= TOL[torch.float16]

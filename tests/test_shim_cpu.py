@@ -14,7 +14,7 @@ def raises(msg, fn, *a):
 
 
 def test_drop_in_module_names():
-    for name in ("linear", "bmm", "fp16_matmul", "bf16_matmul", "fp32_matmul"):
+    for name in ("linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul"):
         assert getattr(cmpext3, name) is getattr(cx, name)
 
 
@@ -51,3 +51,16 @@ def test_set_path_validation():
     cx._set_path("auto")
     with pytest.raises(RuntimeError, match="unknown path"):
         cx._set_path("fast")
+
+
+def test_conv2d_checks():
+    x = torch.zeros(1, 4, 3, 3)
+    w = torch.zeros(6, 4, 1, 1)
+    raises(r"Input must be 4D \(NCHW\)", cx.conv2d, torch.zeros(4, 3, 3), w)
+    raises(r"Weight must be 4D", cx.conv2d, x, torch.zeros(6, 4))
+    raises("groups=1", lambda: cx.conv2d(x, w, None, 1, 0, 1, 2))
+    raises("Input channels mismatch weight channels", cx.conv2d, x, torch.zeros(6, 5, 1, 1))
+    raises("1x1, stride 1, padding 0", cx.conv2d, x, torch.zeros(6, 4, 3, 3))
+    raises("1x1, stride 1, padding 0", lambda: cx.conv2d(x, w, None, 2))
+    raises("1x1, stride 1, padding 0", lambda: cx.conv2d(x, w, None, (1, 1), (0, 1)))
+    raises("expects CUDA tensors", cx.conv2d, x, w)

@@ -199,7 +199,10 @@ bool tma_ok_16bit(const Gemm& g) {
 // the packed row length K and C need 16-byte alignment.
 bool tma_ok_f32(const Gemm& g) {
   const bool a_ok = (g.K * 4) % 16 == 0;
-  const bool b_ok = a_ok;  // B is re-packed K-major ([N][K]) by the split pre-pass
+  // B is re-packed K-major ([N][K]) by the split pre-pass; a [K,N] source is
+  // transposed on the way by a float4 kernel (N, ldb multiples of 4, aligned).
+  const bool b_ok = a_ok && (g.b_kmajor || (g.N % 4 == 0 && g.ldb % 4 == 0 && aligned16(g.B) &&
+                                            (g.batch <= 1 || g.sb % 4 == 0)));
   const bool c_ok = aligned16(g.C) && (g.ldc * 4) % 16 == 0 && (g.batch <= 1 || (g.sc * 4) % 16 == 0);
   return a_ok && b_ok && c_ok;
 }

@@ -472,6 +472,36 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
+__device__ __forceinline__ void split4(const float4 x, float4& h, float4& l) {
+  h.x = tf32_rna(x.x);
+  h.y = tf32_rna(x.y);
+  h.z = tf32_rna(x.z);
+  h.w = tf32_rna(x.w);
+  l.x = tf32_rna(x.x - h.x);
+  l.y = tf32_rna(x.y - h.y);
+  l.z = tf32_rna(x.z - h.z);
+  l.w = tf32_rna(x.w - h.w);
+}
+
+// X [rows][cols] (row stride ld) -> packed hi, lo [rows][cols].  Vector
+// form: cols % 4 == 0, ld % 4 == 0 and X 16-byte aligned.
+__global__ void split_tf32_vec_kernel(const float* __restrict__ X, float* __restrict__ hi, float* __restrict__ lo,
+                                      long long rows, long long cols, long long ld, long long sx) {
+  const long long b = blockIdx.y;
+  const long long c4 = cols / 4, n4 = rows * c4;
+  const float* xb = X + b * sx;
+  float4* hb = reinterpret_cast<float4*>(hi + b * rows * cols);
+  float4* lb = reinterpret_cast<float4*>(lo + b * rows * cols);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / c4, c = i - r * c4;
+    const float4 x = __ldcs(reinterpret_cast<const float4*>(xb + r * ld) + c);
+    float4 h, l;
+    split4(x, h, l);
+    __stcs(hb + i, h);
+    __stcs(lb + i, l);
+  }
+}
+
 __global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict__ hi, float* __restrict__ lo,
                                   long long rows, long long cols, long long ld, long long sx) {
   const long long b = blockIdx.y;
@@ -488,35 +518,50 @@ __global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict
   }
 }
 
-// Same split, writing the transpose ([cols][rows]) through a 32x32 shared
-// tile so both the reads and the writes are coalesced.
-__global__ void split_tf32_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
-                                            float* __restrict__ lo, long long rows, long long cols, long long ld,
-                                            long long sx) {
-  __shared__ float th[32][33];
-  __shared__ float tl[32][33];
+// Same split, writing the transpose ([cols][rows]) through 64x64 shared
+// tiles; float4 reads along cols and float4 writes along rows (vector form:
+// rows % 4 == 0, cols % 4 == 0, ld % 4 == 0, X 16-byte aligned).
+__global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float* __restrict__ X,
+                                                                   float* __restrict__ hi, float* __restrict__ lo,
+                                                                   long long rows, long long cols, long long ld,
+                                                                   long long sx) {
+  __shared__ float th[64][65];
+  __shared__ float tl[64][65];
   const long long b = blockIdx.z;
   const float* xb = X + b * sx;
   float* hb = hi + b * rows * cols;
   float* lb = lo + b * rows * cols;
-  const long long r0 = (long long)blockIdx.y * 32, c0 = (long long)blockIdx.x * 32;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const long long r = r0 + i, c = c0 + threadIdx.x;
-    float h = 0.0f, l = 0.0f;
-    if (r < rows && c < cols) {
-      const float x = xb[r * ld + c];
-      h = tf32_rna(x);
-      l = tf32_rna(x - h);
-    }
-    th[i][threadIdx.x] = h;
-    tl[i][threadIdx.x] = l;
+  const long long r0 = (long long)blockIdx.y * 64, c0 = (long long)blockIdx.x * 64;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {  // 64 rows x 16 float4
+    const int e = t + it * 256;
+    const int rr = e >> 4, cc = (e & 15) * 4;
+    const long long r = r0 + rr, c = c0 + cc;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < rows && c < cols) x = __ldcs(reinterpret_cast<const float4*>(xb + r * ld + c));
+    float4 h, l;
+    split4(x, h, l);
+    th[rr][cc] = h.x;
+    th[rr][cc + 1] = h.y;
+    th[rr][cc + 2] = h.z;
+    th[rr][cc + 3] = h.w;
+    tl[rr][cc] = l.x;
+    tl[rr][cc + 1] = l.y;
+    tl[rr][cc + 2] = l.z;
+    tl[rr][cc + 3] = l.w;
   }
   __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const long long c = c0 + i, r = r0 + threadIdx.x;
-    if (r < rows && c < cols) {
-      hb[c * rows + r] = th[threadIdx.x][i];
-      lb[c * rows + r] = tl[threadIdx.x][i];
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {  // 64 output rows (= input cols) x 16 float4 along input rows
+    const int e = t + it * 256;
+    const int cc = e >> 4, rr = (e & 15) * 4;
+    const long long c = c0 + cc, r = r0 + rr;
+    if (c < cols && r < rows) {
+      __stcs(reinterpret_cast<float4*>(hb + c * rows + r),
+             make_float4(th[rr][cc], th[rr + 1][cc], th[rr + 2][cc], th[rr + 3][cc]));
+      __stcs(reinterpret_cast<float4*>(lb + c * rows + r),
+             make_float4(tl[rr][cc], tl[rr + 1][cc], tl[rr + 2][cc], tl[rr + 3][cc]));
     }
   }
 }
@@ -524,17 +569,25 @@ __global__ void split_tf32_transpose_kernel(const float* __restrict__ X, float* 
 
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
                               int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
+  const bool vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && cols % 4 == 0 && ld % 4 == 0 &&
+                   (batch <= 1 || sx % 4 == 0);
   if (transpose) {
-    const dim3 grid{unsigned((cols + 31) / 32), unsigned((rows + 31) / 32), unsigned(batch)};
-    split_tf32_transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(X, hi, lo, rows, cols, ld, sx);
+    // The transpose is only needed for [K,N] B, whose packed copy is used by
+    // the tensor-core path: K (= rows) % 4 == 0 holds there.
+    if (!vec || rows % 4 != 0) return cudaErrorInvalidValue;
+    const dim3 grid{unsigned((cols + 63) / 64), unsigned((rows + 63) / 64), unsigned(batch)};
+    split_tf32_transpose_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
     return cudaGetLastError();
   }
-  const long long n = rows * cols;
+  const long long n = vec ? rows * cols / 4 : rows * cols;
   long long blocks = (n + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
-  split_tf32_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
+  if (vec)
+    split_tf32_vec_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
+  else
+    split_tf32_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
   return cudaGetLastError();
 }
 

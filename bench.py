@@ -432,7 +432,7 @@ def main(argv=None):
     ap.add_argument("--config", type=int, default=3, choices=[2, 3, 4, 5])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="all-gather C to every rank (N>1)")
-    ap.add_argument("--chunks", type=int, default=4, help="row chunks for the overlapped gather")
+    ap.add_argument("--chunks", type=int, default=1, help="row chunks for the overlapped gather (1 = in place)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true",

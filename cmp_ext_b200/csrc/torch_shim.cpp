@@ -273,6 +273,37 @@ torch::Tensor conv2d(torch::Tensor input, torch::Tensor weight, c10::optional<to
   return output;
 }
 
+// a [M,K] @ b [K,N] written into `out` (a row-major [M,N] view whose rows
+// may be a slice of a larger tensor: row stride out.stride(0), unit column
+// stride).  Used by the M-sharded path to compute straight into its rows of
+// the gathered output.
+void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out) {
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "matmul_into: 2-D tensors expected");
+  TORCH_CHECK(a.is_cuda() && b.device() == a.device() && out.device() == a.device(), "matmul_into: one CUDA device");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type() && out.scalar_type() == a.scalar_type(), "Dtype mismatch");
+  TORCH_CHECK(a.size(1) == b.size(0), "Contracting dimension (K) mismatch");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == b.size(1), "matmul_into: output shape mismatch");
+  TORCH_CHECK(out.stride(1) == 1, "matmul_into: output rows must be contiguous");
+  const int dt = dtype_code(a.scalar_type());
+  TORCH_CHECK(dt >= 0, "Unsupported dtype");
+  c10::cuda::CUDAGuard guard(a.device());
+  a = a.contiguous();
+  b = b.contiguous();
+  cmpx_gemm_args args = base_args(dt);
+  args.A = a.data_ptr();
+  args.B = b.data_ptr();
+  args.C = out.data_ptr();
+  args.M = a.size(0);
+  args.N = b.size(1);
+  args.K = a.size(1);
+  args.lda = args.K;
+  args.ldb = args.N;
+  args.ldc = out.stride(0);
+  args.b_layout = CMPX_B_KN;
+  args.path = g_forced_path;
+  check_status(cmpx_gemm(&args, current_stream()), "matmul_into");
+}
+
 torch::Tensor fp16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kHalf, "fp16_matmul"); }
 torch::Tensor bf16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kBFloat16, "bf16_matmul"); }
 torch::Tensor fp32_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kFloat, "fp32_matmul"); }
@@ -289,6 +320,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp16_matmul", &fp16_matmul, "a[M,K] @ b[K,N] in fp16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
   m.def("bf16_matmul", &bf16_matmul, "a[M,K] @ b[K,N] in bf16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
   m.def("fp32_matmul", &fp32_matmul, "a[M,K] @ b[K,N] in fp32 (3xTF32)", py::arg("a"), py::arg("b"));
+  m.def("_matmul_into", &matmul_into, "a @ b written into out (internal)", py::arg("a"), py::arg("b"),
+        py::arg("out"));
   m.def("_set_path", &set_path, "force a kernel path for testing: auto, tc, skinny, simt");
   m.def("_version", []() { return std::string(cmpx_version()); });
 }

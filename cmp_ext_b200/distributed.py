@@ -38,11 +38,16 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
     a_shard: this rank's rows of A, as given by ``shard_rows(M, world, rank)``.
     M: total rows (needed when gathering; defaults to a_shard rows x world,
        which is right when M divides evenly).
+    gather: each rank computes straight into its row block of the full
+       output and the blocks are all-gathered in place over NCCL -- no
+       staging buffer and no extra copy.
     chunks: with gather=True, split the shard into this many row chunks and
-       all-gather chunk i while chunk i+1 is being multiplied.
+       all-gather chunk i (through a staging buffer) while chunk i+1 is
+       multiplied.
     op: the per-shard GEMM (defaults to cmp_ext_b200's *_matmul for the dtype;
        tests on CPU pass torch.matmul).
     """
+    op_is_default = op is None
     op = op or default_op(a_shard.dtype)
     if not gather:
         return op(a_shard, b)
@@ -70,7 +75,14 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
     S = sizes[0]
     chunks = max(1, min(chunks, S))
     if chunks == 1:
-        dist.all_gather_into_tensor(out, op(a_shard, b), group=group)
+        mine = out[rank * S:(rank + 1) * S]
+        if op_is_default and a_shard.is_cuda:
+            import cmp_ext_b200 as cx
+
+            cx._matmul_into(a_shard, b, mine)
+        else:
+            mine.copy_(op(a_shard, b))
+        dist.all_gather_into_tensor(out, mine, group=group)  # in place: input is this rank's block of out
         return out
     # Chunked: all-gather chunk i (into a staging buffer laid out
     # [chunk][rank][rows]) while the next chunk computes; then scatter rows

@@ -127,7 +127,10 @@ def dist_setup(args):
     if world > 1 and not dist.is_initialized():
         if args.impl == "ours":
             torch.cuda.set_device(local)
-            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            import datetime
+
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                    timeout=datetime.timedelta(seconds=180))
         else:
             dist.init_process_group("gloo")
     return world, rank, local

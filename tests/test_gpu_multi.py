@@ -1,0 +1,64 @@
+"""M-sharded matmul over NCCL on two GPUs (one process per GPU, launched as
+child processes).  Skipped on a one-GPU box.  Checks that every rank ends up
+with the full product (in-place gather and chunked gather), equal to the
+product one GPU computes."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+
+WORKER = r"""
+import os, sys, torch, torch.distributed as dist
+sys.path.insert(0, os.environ["REPO"])
+from cmp_ext_b200.distributed import shard_rows, sharded_matmul
+import cmp_ext_b200 as cx
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+import datetime
+dist.init_process_group("nccl", device_id=torch.device("cuda", rank), timeout=datetime.timedelta(seconds=60))
+g = torch.Generator(device="cuda").manual_seed(0)
+M, K, N = 2048, 1024, 768
+A = torch.randn(M, K, generator=g, device="cuda").bfloat16()
+B = (torch.randn(K, N, generator=g, device="cuda") * 0.05).bfloat16()
+full = cx.bf16_matmul(A, B)
+r0, r1 = shard_rows(M, world, rank)
+for chunks in (1, 4):
+    C = sharded_matmul(A[r0:r1].contiguous(), B, M=M, gather=True, chunks=chunks)
+    torch.cuda.synchronize()
+    err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
+    assert err <= 2 ** -7, (chunks, err)
+mine = sharded_matmul(A[r0:r1].contiguous(), B)
+assert torch.equal(mine, full[r0:r1]) or ((mine.float() - full[r0:r1].float()).abs().max() / full.float().abs().max()).item() <= 2 ** -7
+dist.barrier()
+dist.destroy_process_group()
+print("rank", rank, "ok")
+"""
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_sharded_gather_two_gpus(cuda, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER)
+    env = dict(os.environ, REPO=REPO, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr=127.0.0.1", f"--master-port={_port()}", str(script)],
+                       env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    assert r.stdout.count(" ok") == 2

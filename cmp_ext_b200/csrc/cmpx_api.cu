@@ -317,7 +317,7 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
     const uint32_t mn = uint32_t(skinny_mn(g.M));
     CUtensorMap tB, tA;
     st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 128)
-                    : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
+                    : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 128);
     if (st != CMPX_OK) return st;
     st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.a_bcast ? 1 : g.batch, g.lda, g.sa, 64, mn);
     if (st != CMPX_OK) return st;

@@ -15,9 +15,9 @@
 // and stores.  The counters are left at zero for the next launch.
 //
 // Shared-memory operand layouts (128-byte swizzle, written by TMA):
-//   B slab, [K,N] source: 2 chunks of [64 K rows][64 N] (MN-major, LBO 8192, SBO 1024)
-//   B slab, [N,K] source: [128 N rows][64 K]            (K-major, SBO 1024)
-//   A tile            : [MN rows][64 K]                  (K-major, SBO 1024)
+//   B slab, [K,N] source: 2 chunks of [128 K rows][64 N] (MN-major, LBO 16384, SBO 1024)
+//   B slab, [N,K] source: 2 atoms of [128 N rows][64 K]   (K-major, SBO 1024, atoms 16 KB apart)
+//   A tile            : 2 atoms of [MN rows][64 K]        (K-major, SBO 1024, atoms MN*128 B apart)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -52,9 +52,12 @@ struct SkParams {
 // ([K,N] layout) before moving down to the next k-block.
 template <int FMT, bool B_KMAJOR, int MN, int NS>
 struct SkCfg {
-  static constexpr int BK = 64;
-  static constexpr int SUB_BYTES = 128 * 128;       // 128 N x 64 K x 2 B
-  static constexpr int ATILE_BYTES = MN * 128;      // MN rows x 64 K x 2 B
+  // 128 K rows per k-block: in this kernel's walk down a column strip of B,
+  // TMA boxes of 128 rows stream from HBM at ~6.5 TB/s where 64-row boxes
+  // reach only ~3.5 (measured on a B200 with a no-compute TMA stream).
+  static constexpr int BK = 128;
+  static constexpr int SUB_BYTES = 128 * 256;       // 128 N x 128 K x 2 B (two 16 KB boxes / atoms)
+  static constexpr int ATILE_BYTES = MN * 256;      // MN rows x 128 K x 2 B (two 64-K atoms)
   static constexpr int STAGE_BYTES = SUB_BYTES + ATILE_BYTES;
   static constexpr int STAGES_FIT = (225 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 16 ? 16 : STAGES_FIT;
@@ -156,13 +159,14 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sB = smem + size_t(stage) * Cfg::STAGE_BYTES;
           uint8_t* sA = sB + Cfg::SUB_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
-          if (B_KMAJOR) {
-            tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0 + sub * 128, b);
-          } else {
-            tma_load_3d(sB, &tmB, &full_bar[stage], n0 + sub * 128, k0, b);
-            tma_load_3d(sB + 8192, &tmB, &full_bar[stage], n0 + sub * 128 + 64, k0, b);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (B_KMAJOR)  // [N,K]: box = 64 K x 128 rows -> K-major atom h (K 64h..64h+63)
+              tma_load_3d(sB + h * 16384, &tmB, &full_bar[stage], k0 + 64 * h, n0 + sub * 128, b);
+            else  // [K,N]: box = 64 N x 128 K rows -> MN-major chunk h (N 64h..64h+63)
+              tma_load_3d(sB + h * 16384, &tmB, &full_bar[stage], n0 + sub * 128 + 64 * h, k0, b);
+            tma_load_3d(sA + h * (MN * 128), &tmA, &full_bar[stage], k0 + 64 * h, 0, p.a_bcast ? 0 : b);
           }
-          tma_load_3d(sA, &tmA, &full_bar[stage], k0, 0, p.a_bcast ? 0 : b);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -216,10 +220,13 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t b_addr = smem_u32(smem + size_t(stage) * Cfg::STAGE_BYTES);
             const uint32_t a_addr = b_addr + Cfg::SUB_BYTES;
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t a_desc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
-              const uint64_t slab_desc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
-                                                  : make_sdesc_sw128(b_addr + ks * 2048, 8192, 1024);
+            for (int ks = 0; ks < 8; ++ks) {
+              // 16 K per MMA: K-major operands step 32 B inside a 64-K atom,
+              // then move to the next atom; the MN-major slab steps 16 rows.
+              const uint64_t a_desc = make_sdesc_sw128(a_addr + (ks >> 2) * (MN * 128) + (ks & 3) * 32, 16, 1024);
+              const uint64_t slab_desc =
+                  B_KMAJOR ? make_sdesc_sw128(b_addr + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024)
+                           : make_sdesc_sw128(b_addr + ks * 2048, 16384, 1024);
               mma_f16(d_tmem + sub * MN, slab_desc, a_desc, Cfg::IDESC, (kb != kb0 || ks != 0) ? 1u : 0u);
             }
             mma_commit(&empty_bar[stage]);
@@ -367,7 +374,7 @@ cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorM
   p.ldc = g.ldc;
   p.stride_c = g.sc;
   p.n_tiles = int((g.N + 128 * NS - 1) / (128 * NS));
-  p.kbt = int((g.K + 63) / 64);
+  p.kbt = int((g.K + Cfg::BK - 1) / Cfg::BK);
   p.units = 1LL * g.batch * p.n_tiles * p.kbt;
   const long long grid = p.units < dev.num_sms ? p.units : dev.num_sms;
   p.counters = reinterpret_cast<int*>(ws);
@@ -420,7 +427,7 @@ int skinny_ns(const Gemm& g, const DeviceInfo& dev) {
     if (e != nullptr && (e[0] == '1' || e[0] == '2' || e[0] == '4' || e[0] == '8') && e[1] == 0) forced = e[0] - '0';
   }
   if (forced > 0 && forced * mn <= 256) return forced;
-  const int64_t kbt = (g.K + 63) / 64;
+  const int64_t kbt = (g.K + 127) / 128;
   for (int ns : {2}) {
     if (ns * mn > 256) continue;
     const int64_t w = 128 * ns;
@@ -556,7 +563,7 @@ extern "C" CMPX_API int cmpx_matmul_skinny_noalloc(int dtype, const void* A, con
 
   CUtensorMap tB, tA;
   st = g.b_kmajor ? encode_tmap_3d(&tB, dtype, B, K, N, 1, K, g.sb, 64, 128)
-                  : encode_tmap_3d(&tB, dtype, B, N, K, 1, N, g.sb, 64, 64);
+                  : encode_tmap_3d(&tB, dtype, B, N, K, 1, N, g.sb, 64, 128);
   if (st != CMPX_OK) return st;
   st = encode_tmap_3d(&tA, dtype, A, K, M, 1, K, g.sa, 64, uint32_t(skinny_mn(M)));
   if (st != CMPX_OK) return st;

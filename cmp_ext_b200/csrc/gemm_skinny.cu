@@ -362,7 +362,7 @@ cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorM
   using Cfg = SkCfg<FMT, B_KMAJOR, MN, NS>;
   auto kern = gemm_skinny_kernel<FMT, B_KMAJOR, MN, NS>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM));
+  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM));
   if (e != cudaSuccess) return e;
   SkParams p;
   p.C = g.C;
@@ -413,12 +413,13 @@ cudaError_t launch_sk_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap
 
 int skinny_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-// Sub-slabs per work unit: 2 when that leaves every CTA at least four units
-// and pads N by at most 1/8, else 1.  Measured on config 4 (16 x 28672 x
-// 8192 fp16, B200): 1 -> 68%, 2 -> 79%, 4 -> 72%, 8 -> 58% of HBM copy
-// bandwidth, so wider units are not chosen automatically.
-// CMPX_SKINNY_NS=1|2|4|8 overrides (tuning experiments).
+// Sub-slabs per work unit.  Measured on config 4 (16 x 28672 x 8192 fp16,
+// B200, 128-row k-blocks): 1 sub-slab 5221 GB/s single launch / 5657
+// back-to-back, 2 -> 5082 / 5452, 4 -> 4596 / 4933, so one 128-column slab
+// per unit is used.  CMPX_SKINNY_NS=1|2|4|8 overrides (tuning experiments;
+// NS * M rounded up must fit 256 TMEM columns).
 int skinny_ns(const Gemm& g, const DeviceInfo& dev) {
+  (void)dev;
   const int mn = skinny_mn(g.M);
   static int forced = -1;
   if (forced < 0) {
@@ -427,14 +428,6 @@ int skinny_ns(const Gemm& g, const DeviceInfo& dev) {
     if (e != nullptr && (e[0] == '1' || e[0] == '2' || e[0] == '4' || e[0] == '8') && e[1] == 0) forced = e[0] - '0';
   }
   if (forced > 0 && forced * mn <= 256) return forced;
-  const int64_t kbt = (g.K + 127) / 128;
-  for (int ns : {2}) {
-    if (ns * mn > 256) continue;
-    const int64_t w = 128 * ns;
-    const int64_t tiles = (g.N + w - 1) / w;
-    const int64_t pad = tiles * w - g.N;
-    if (pad * 8 <= g.N && g.batch * tiles * kbt >= 4LL * dev.num_sms) return ns;
-  }
   return 1;
 }
 

@@ -423,7 +423,7 @@ cudaError_t launch_tc_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   using Cfg = TcCfg<FMT, B_KMAJOR, BN, STAGES>;
   auto kern = gemm_tc_kernel<FMT, B_KMAJOR, BN, STAGES>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM));
+  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM));
   if (e != cudaSuccess) return e;
   TcParams p;
   p.C = g.C;

@@ -99,3 +99,21 @@ int encode_tmap_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, 
                    uint64_t ld, uint64_t bstride, uint32_t box_inner, uint32_t box_rows);
 
 }  // namespace cmpx
+
+namespace cmpx {
+// Sets a kernel's dynamic shared-memory limit once per device (the attribute
+// is per function and device; setting it on every launch costs host time that
+// shows up in short kernels' latency).
+template <typename KernelPtr>
+cudaError_t set_smem_once(KernelPtr kern, int bytes) {
+  static unsigned long long done = 0;  // bit d: set on device d
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit != 0 && (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit != 0) __atomic_fetch_or(&done, bit, __ATOMIC_RELEASE);
+  return e;
+}
+}  // namespace cmpx

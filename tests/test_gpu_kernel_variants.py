@@ -21,3 +21,14 @@ def test_tile_kernel_variant(cuda, pair, streamk):
                         os.path.join(HERE, "test_gpu_parity.py"), "-k", "tc_path or batched or bias"],
                        env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("ns", ["2", "4"])
+def test_skinny_unit_width_variant(cuda, ns):
+    """The skinny kernel with wider work units (2 / 4 sub-slabs), which the
+    dispatcher does not pick by default but CMPX_SKINNY_NS can select."""
+    env = dict(os.environ, CMPX_SKINNY_NS=ns)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.join(HERE, "test_gpu_parity.py"), "-k", "skinny"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

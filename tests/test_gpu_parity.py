@@ -94,7 +94,7 @@ def test_tc_path_bias(cuda, b_layout):
 
 
 # ------------------------------------------------------------ skinny path
-# (16, 28672, 512), (16, 8192, 8192) and (40, 4096, 16384) take two sub-slabs per work unit
+# large-N cases: (16, 28672, 512), (16, 8192, 8192), (40, 4096, 16384)
 SK_SHAPES = [(1, 128, 64), (7, 1000, 200), (16, 4096, 1024), (17, 256, 8192), (32, 520, 640), (33, 384, 256),
              (64, 2048, 2048), (16, 28672, 512), (16, 8192, 8192), (40, 4096, 16384)]
 

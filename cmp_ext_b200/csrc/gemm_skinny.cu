@@ -362,7 +362,8 @@ cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorM
   using Cfg = SkCfg<FMT, B_KMAJOR, MN, NS>;
   auto kern = gemm_skinny_kernel<FMT, B_KMAJOR, MN, NS>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
-  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM));
+  static unsigned long long smem_set = 0;  // one flag word per kernel instantiation
+  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
   if (e != cudaSuccess) return e;
   SkParams p;
   p.C = g.C;

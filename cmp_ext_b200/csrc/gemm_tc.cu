@@ -423,7 +423,8 @@ cudaError_t launch_tc_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   using Cfg = TcCfg<FMT, B_KMAJOR, BN, STAGES>;
   auto kern = gemm_tc_kernel<FMT, B_KMAJOR, BN, STAGES>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
-  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM));
+  static unsigned long long smem_set = 0;  // one flag word per kernel instantiation
+  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
   if (e != cudaSuccess) return e;
   TcParams p;
   p.C = g.C;

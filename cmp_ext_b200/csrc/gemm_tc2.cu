@@ -430,7 +430,8 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
   using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES>;
   auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
-  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM));
+  static unsigned long long smem_set = 0;  // one flag word per kernel instantiation
+  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
   if (e != cudaSuccess) return e;
   Tc2Params p;
   p.C = g.C;

@@ -103,10 +103,10 @@ int encode_tmap_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, 
 namespace cmpx {
 // Sets a kernel's dynamic shared-memory limit once per device (the attribute
 // is per function and device; setting it on every launch costs host time that
-// shows up in short kernels' latency).
+// shows up in short kernels' latency).  `done` must be a flag word owned by
+// that one kernel (a static in its launcher): bit d = set on device d.
 template <typename KernelPtr>
-cudaError_t set_smem_once(KernelPtr kern, int bytes) {
-  static unsigned long long done = 0;  // bit d: set on device d
+cudaError_t set_smem_once(KernelPtr kern, int bytes, unsigned long long& done) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;

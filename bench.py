@@ -378,11 +378,11 @@ def run_ours(args):
         hC = torch.empty((m, cfg.N), dtype=cfg.dtype).pin_memory()
         e_steps = max(3, min(args.steps, 10))
 
+        from cmp_ext_b200.host import host_matmul
+
         def e2e_step():
-            dA = hA.to(device, non_blocking=True)
-            dB = hB.to(device, non_blocking=True)
-            out = op(dA, dB)
-            hC.copy_(out, non_blocking=True)
+            # host in, host out; uploads, GEMMs and downloads overlapped in row chunks
+            host_matmul(hA, hB, out=hC, chunks=8, device=device)
 
         for _ in range(2):
             e2e_step()
@@ -399,7 +399,7 @@ def run_ours(args):
         d2h = hC.numel() * e
         ev = (step_bytes_job / (e_ms / 1e3) / 1e9) if unit == "GB/s" else (step_flops / (e_ms / 1e3) / 1e12)
         e2e = {"value": ev, "unit": unit, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-               "ms_per_step": e_ms, "api": f"cmp_ext_b200.{op.__name__} (pinned host in/out)"}
+               "ms_per_step": e_ms, "api": "cmp_ext_b200.host.host_matmul (pinned host in/out, 8 row chunks)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

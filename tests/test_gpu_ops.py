@@ -79,3 +79,21 @@ def test_shared_a_and_row_bias_cabi(cuda, path):
     torch.cuda.synchronize()
     want = torch.matmul(A.float(), Bm.float()) + bias.float()[None, :, None]
     assert _err(C, want) <= TOL[torch.float16]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_host_matmul(cuda, dtype, chunks):
+    from cmp_ext_b200.host import host_matmul
+
+    g = torch.Generator().manual_seed(12)
+    a = torch.randn(1000, 264, generator=g).to(dtype).pin_memory()
+    b = (torch.randn(264, 520, generator=g) * 0.1).to(dtype).pin_memory()
+    c = host_matmul(a, b, chunks=chunks)
+    torch.cuda.synchronize()
+    assert not c.is_cuda and c.shape == (1000, 520)
+    assert _err(c, a.float() @ b.float()) <= TOL[dtype]
+    c2 = torch.zeros_like(c).pin_memory()
+    host_matmul(a, b, out=c2, chunks=chunks)
+    torch.cuda.synchronize()
+    assert torch.equal(c, c2)

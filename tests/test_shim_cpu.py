@@ -64,3 +64,14 @@ def test_conv2d_checks():
     raises("1x1, stride 1, padding 0", lambda: cx.conv2d(x, w, None, 2))
     raises("1x1, stride 1, padding 0", lambda: cx.conv2d(x, w, None, (1, 1), (0, 1)))
     raises("expects CUDA tensors", cx.conv2d, x, w)
+
+
+def test_host_matmul_argument_checks():
+    from cmp_ext_b200.host import host_matmul
+
+    with pytest.raises(ValueError, match="2-D"):
+        host_matmul(torch.zeros(2, 3, 4), torch.zeros(4, 5))
+    with pytest.raises(ValueError, match="Dtype mismatch"):
+        host_matmul(torch.zeros(2, 3), torch.zeros(3, 4, dtype=torch.float16))
+    with pytest.raises(ValueError, match="Contracting"):
+        host_matmul(torch.zeros(2, 3), torch.zeros(4, 4))

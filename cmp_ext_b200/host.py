@@ -36,7 +36,12 @@ def host_matmul(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = Non
         raise ValueError("Contracting dimension (K) mismatch")
     M, K = a.shape
     N = b.shape[1]
-    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device("cuda", device).index)
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        dev = torch.device("cuda", device)
+    else:
+        dev = torch.device(device)
     a = a.contiguous()
     b = b.contiguous()
     if out is None:

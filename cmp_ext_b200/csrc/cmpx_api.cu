@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 #include "internal.h"
@@ -149,7 +150,7 @@ int validate(const cmpx_gemm_args* a) {
   if (a->path < CMPX_PATH_AUTO || a->path > CMPX_PATH_SIMT) return CMPX_ERR_INVALID_ARG;
   if (a->batch < 0 || a->M < 0 || a->N < 0 || a->K < 0) return CMPX_ERR_INVALID_ARG;
   const int64_t lim = (int64_t(1) << 31) - 1;
-  if (a->M > lim || a->N > lim || a->K > lim || a->batch > 65535) return CMPX_ERR_UNSUPPORTED;
+  if (a->M > lim || a->N > lim || a->K > lim) return CMPX_ERR_UNSUPPORTED;
   if (a->batch == 0 || a->M == 0 || a->N == 0) return CMPX_OK;
   if (a->C == nullptr) return CMPX_ERR_INVALID_ARG;
   if (a->ldc < a->N) return CMPX_ERR_INVALID_ARG;
@@ -428,7 +429,25 @@ int cmpx_matmul_f32(const float* A, const float* B, float* C, int64_t M, int64_t
   return packed_matmul(CMPX_F32, A, B, C, M, N, K, stream);
 }
 
-int cmpx_gemm(const cmpx_gemm_args* args, cmpx_stream_t stream) { return run_gemm(args, stream); }
+int cmpx_gemm(const cmpx_gemm_args* args, cmpx_stream_t stream) {
+  // Kernels index the batch with a grid dimension (at most 65535); larger
+  // batches run as consecutive slices of it.
+  constexpr int64_t kMaxBatch = 65535;
+  if (args == nullptr || args->batch <= kMaxBatch) return run_gemm(args, stream);
+  const int st = validate(args);
+  if (st != CMPX_OK) return st;
+  const int64_t E = args->dtype == CMPX_F32 ? 4 : 2;
+  for (int64_t b0 = 0; b0 < args->batch; b0 += kMaxBatch) {
+    cmpx_gemm_args part = *args;
+    part.batch = std::min<int64_t>(kMaxBatch, args->batch - b0);
+    part.A = static_cast<const char*>(args->A) + b0 * args->stride_a * E;
+    part.B = static_cast<const char*>(args->B) + b0 * args->stride_b * E;
+    part.C = static_cast<char*>(args->C) + b0 * args->stride_c * E;
+    const int r = run_gemm(&part, stream);
+    if (r != CMPX_OK) return r;
+  }
+  return CMPX_OK;
+}
 
 size_t cmpx_gemm_workspace_size(const cmpx_gemm_args* args) {
   if (validate(args) != CMPX_OK) return 0;

@@ -97,3 +97,12 @@ def test_host_matmul(cuda, dtype, chunks):
     host_matmul(a, b, out=c2, chunks=chunks)
     torch.cuda.synchronize()
     assert torch.equal(c, c2)
+
+
+def test_bmm_batch_beyond_grid_limit(cuda):
+    """More batch entries than a grid dimension holds (65535): processed in
+    slices, as the reference's per-batch loop would."""
+    a = torch.randn(70000, 2, 8, device="cuda", dtype=torch.float16)
+    b = torch.randn(70000, 8, 4, device="cuda", dtype=torch.float16)
+    c = cx.bmm(a, b)
+    assert _err(c, torch.bmm(a.float(), b.float())) <= TOL[torch.float16]

@@ -209,11 +209,11 @@ def torch_cpu_sample(cfg, rows: int):
     return 2.0 * rows * cfg.N * cfg.K / dt / 1e12, dt, threads
 
 
-def config_block(cfg, world, gather):
+def config_block(cfg, world, gather, transport="nccl"):
     return {"workload": f"config{cfg.cid}: {cfg.name}", "M": cfg.M, "N": cfg.N, "K": cfg.K,
             "a": "N(0,1)" if cfg.a_dist == "normal" else "U(-1,1)",
             "b": f"N(0,{cfg.b_std})" if cfg.a_dist == "normal" else "U(-1,1)",
-            "parallelism": f"M-shard x{world}" + (" + all-gather" if gather else ""),
+            "parallelism": f"M-shard x{world}" + ((" + all-gather (" + transport + ")") if gather else ""),
             "l2": "inputs larger than L2 (126 MB) per GPU" if cfg.bytes(cfg.M // world) > 126e6
             else "L2 flushed between steps"}
 
@@ -282,14 +282,17 @@ def run_ours(args):
 
     gather = args.gather and world > 1
     if gather:
-        from cmp_ext_b200.distributed import sharded_matmul
-        Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
+        from cmp_ext_b200.distributed import gather_output, sharded_matmul
+        if args.transport == "nvlink":
+            Cfull = gather_output(cfg.M, cfg.N, cfg.dtype, device)
+        else:
+            Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
 
     def step():
         if flush is not None:
             flush.fill_(1)
         if gather:
-            sharded_matmul(A, B, M=cfg.M, gather=True, chunks=args.chunks, out=Cfull)
+            sharded_matmul(A, B, M=cfg.M, gather=True, chunks=args.chunks, out=Cfull, transport=args.transport)
         else:
             op(A, B)
 
@@ -420,7 +423,7 @@ def run_ours(args):
         line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": cfg.dtype_name, "data": "synthetic (seeded, drawn on device)",
-                "config": config_block(cfg, world, gather),
+                "config": config_block(cfg, world, gather, args.transport),
                 "roofline": {"bound": rbound, "kernel": kernel_name(cfg), "achieved": achieved, "peak": peak,
                              "peak_source": peak_src, "unit": runit, "frac": achieved / peak,
                              "traffic": traffic, "launch_ms": launch_ms,
@@ -444,6 +447,8 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="all-gather C to every rank (N>1)")
     ap.add_argument("--chunks", type=int, default=1, help="row chunks for the overlapped gather (1 = in place)")
+    ap.add_argument("--transport", default="nccl", choices=["nccl", "nvlink"],
+                    help="gather: NCCL all-gather, or epilogue stores into peers' outputs over NVLink")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true",

@@ -160,6 +160,12 @@ int validate(const cmpx_gemm_args* a) {
     if (a->ldb < (a->b_layout == CMPX_B_KN ? a->N : a->K)) return CMPX_ERR_INVALID_ARG;
   }
   if (a->stride_a < 0 || a->stride_b < 0 || a->stride_c < 0) return CMPX_ERR_INVALID_ARG;
+  if (a->n_peer_C < 0 || a->n_peer_C > kMaxPeerOut) return CMPX_ERR_INVALID_ARG;
+  if (a->n_peer_C > 0) {
+    if (a->peer_C == nullptr) return CMPX_ERR_INVALID_ARG;
+    for (int i = 0; i < a->n_peer_C; ++i)
+      if (a->peer_C[i] == nullptr) return CMPX_ERR_INVALID_ARG;
+  }
   return CMPX_OK;
 }
 
@@ -183,6 +189,8 @@ Gemm to_gemm(const cmpx_gemm_args* a) {
   g.b_kmajor = a->b_layout == CMPX_B_NK ? 1 : 0;
   g.a_bcast = (a->batch > 1 && a->stride_a == 0) ? 1 : 0;
   g.bias_m = a->bias_along_m ? 1 : 0;
+  g.peers.n = a->n_peer_C;
+  for (int i = 0; i < kMaxPeerOut; ++i) g.peers.base[i] = i < a->n_peer_C ? a->peer_C[i] : nullptr;
   return g;
 }
 
@@ -224,7 +232,8 @@ int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
   // The skinny path's counter region holds kSkinnyMaxTiles tiles; without
   // device facts (host-only path queries) assume the narrowest units.
   const int64_t sk_tiles = dev != nullptr ? skinny_tiles(g, *dev) : g.batch * ((g.N + 127) / 128);
-  const bool sk_ok = ok && g.M <= 64 && sk_tiles <= kSkinnyMaxTiles;
+  // (peer outputs are written by the tile kernels only)
+  const bool sk_ok = ok && g.M <= 64 && sk_tiles <= kSkinnyMaxTiles && g.peers.n == 0;
   if (forced == CMPX_PATH_SKINNY) return sk_ok ? CMPX_PATH_SKINNY : -1;
   if (forced == CMPX_PATH_SIMT) return CMPX_PATH_SIMT;
   if (!ok) return CMPX_PATH_SIMT;

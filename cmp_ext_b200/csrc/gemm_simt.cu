@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
                                                         T* __restrict__ C, const T* __restrict__ bias, int M, int N,
                                                         int K, long long lda, long long ldb, long long ldc,
                                                         long long sa, long long sb, long long sc, int b_kmajor,
-                                                        int bias_m) {
+                                                        int bias_m, PeerOut peers) {
   __shared__ float As[SB_K][SB_M + 4];
   __shared__ float Bs[SB_K][SB_N + 4];
   const int tid = threadIdx.x;
@@ -87,17 +87,20 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
       float v = acc[i][j];
       if (bias != nullptr) v += ld_f32(bias + (bias_m ? gm : gn));
       st_f32(C + gm * ldc + gn, v);
+      for (int q = 0; q < peers.n; ++q) st_f32(static_cast<T*>(peers.base[q]) + bz * sc + gm * ldc + gn, v);
     }
   }
 }
 
 template <typename T>
 __global__ void fill_bias_kernel(T* __restrict__ C, const T* __restrict__ bias, long long M, long long N,
-                                 long long ldc, long long sc, int bias_m) {
+                                 long long ldc, long long sc, int bias_m, PeerOut peers) {
   const long long bz = blockIdx.y;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M * N; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / N, c = i - r * N;
-    st_f32(C + bz * sc + r * ldc + c, bias != nullptr ? ld_f32(bias + (bias_m ? r : c)) : 0.0f);
+    const float v = bias != nullptr ? ld_f32(bias + (bias_m ? r : c)) : 0.0f;
+    st_f32(C + bz * sc + r * ldc + c, v);
+    for (int q = 0; q < peers.n; ++q) st_f32(static_cast<T*>(peers.base[q]) + bz * sc + r * ldc + c, v);
   }
 }
 
@@ -116,7 +119,7 @@ cudaError_t simt_t(const Gemm& g, cudaStream_t s) {
   gemm_simt_kernel<T><<<grid, 256, 0, s>>>(reinterpret_cast<const T*>(g.A), reinterpret_cast<const T*>(g.B),
                                            reinterpret_cast<T*>(g.C), reinterpret_cast<const T*>(g.bias), int(g.M),
                                            int(g.N), int(g.K), g.lda, g.ldb, g.ldc, g.sa, g.sb, g.sc, g.b_kmajor,
-                                           g.bias_m);
+                                           g.bias_m, g.peers);
   return cudaGetLastError();
 }
 
@@ -126,7 +129,7 @@ cudaError_t fill_t(const Gemm& g, cudaStream_t s) {
   if (blocks > 4096) blocks = 4096;
   if (blocks < 1) blocks = 1;
   fill_bias_kernel<T><<<dim3(unsigned(blocks), unsigned(g.batch)), 256, 0, s>>>(
-      reinterpret_cast<T*>(g.C), reinterpret_cast<const T*>(g.bias), g.M, g.N, g.ldc, g.sc, g.bias_m);
+      reinterpret_cast<T*>(g.C), reinterpret_cast<const T*>(g.bias), g.M, g.N, g.ldc, g.sc, g.bias_m, g.peers);
   return cudaGetLastError();
 }
 

@@ -38,6 +38,7 @@ struct TcParams {
   int tiles_m, tiles_n, group_m;
   int a_bcast;
   int bias_m;
+  PeerOut peers;
   int* err;
 };
 
@@ -115,7 +116,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
 // falls back to scalar stores.
 template <typename T>
 __device__ __forceinline__ void store_row32(T* crow, const T* bias, float rowb, int col0, int N,
-                                            const uint32_t (&r)[32]) {
+                                            const uint32_t (&r)[32], const PeerOut& po, size_t off) {
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + rowb;
@@ -137,14 +138,18 @@ __device__ __forceinline__ void store_row32(T* crow, const T* bias, float rowb, 
         q.z = pack2(v[g * 8 + 4], v[g * 8 + 5], (T*)nullptr);
         q.w = pack2(v[g * 8 + 6], v[g * 8 + 7], (T*)nullptr);
         *reinterpret_cast<uint4*>(crow + c) = q;
+        for (int pi = 0; pi < po.n; ++pi) *reinterpret_cast<uint4*>(static_cast<T*>(po.base[pi]) + off + c) = q;
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           if (c + i < N) {
+            T h;
             if constexpr (std::is_same<T, __half>::value)
-              crow[c + i] = __float2half_rn(v[g * 8 + i]);
+              h = __float2half_rn(v[g * 8 + i]);
             else
-              crow[c + i] = __float2bfloat16_rn(v[g * 8 + i]);
+              h = __float2bfloat16_rn(v[g * 8 + i]);
+            crow[c + i] = h;
+            for (int pi = 0; pi < po.n; ++pi) static_cast<T*>(po.base[pi])[off + c + i] = h;
           }
       }
     }
@@ -153,11 +158,16 @@ __device__ __forceinline__ void store_row32(T* crow, const T* bias, float rowb, 
     for (int g = 0; g < 8; ++g) {
       const int c = col0 + g * 4;
       if (c + 4 <= N) {
-        *reinterpret_cast<float4*>(crow + c) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
+        const float4 f = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
+        *reinterpret_cast<float4*>(crow + c) = f;
+        for (int pi = 0; pi < po.n; ++pi) *reinterpret_cast<float4*>(static_cast<T*>(po.base[pi]) + off + c) = f;
       } else {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          if (c + i < N) crow[c + i] = v[g * 4 + i];
+          if (c + i < N) {
+            crow[c + i] = v[g * 4 + i];
+            for (int pi = 0; pi < po.n; ++pi) static_cast<T*>(po.base[pi])[off + c + i] = v[g * 4 + i];
+          }
       }
     }
   }
@@ -344,7 +354,8 @@ __global__ void __launch_bounds__(192, 1)
       int b, tm, tn;
       decode_tile(t, p, b, tm, tn);
       const int row = tm * Cfg::BM + q * 32 + lane;
-      OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      const size_t row_off = size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      OutT* crow = C + row_off;
       const OutT* colb = p.bias_m ? nullptr : bias;
       const float rowb = (p.bias_m && bias != nullptr && row < p.M) ? to_f32<OutT>(bias[row]) : 0.0f;
       if constexpr (FMT == 2) {
@@ -380,7 +391,7 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t r[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(racc[c * 32 + i]);
-            store_row32<OutT>(crow, colb, rowb, tn * BN + c * 32, p.N, r);
+            store_row32<OutT>(crow, colb, rowb, tn * BN + c * 32, p.N, r, p.peers, row_off);
           }
         }
       } else {
@@ -400,7 +411,7 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);
           tmem_ld_wait();
-          if (row < p.M) store_row32<OutT>(crow, colb, rowb, tn * BN + c * 32, p.N, r);
+          if (row < p.M) store_row32<OutT>(crow, colb, rowb, tn * BN + c * 32, p.N, r, p.peers, row_off);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
@@ -440,6 +451,7 @@ cudaError_t launch_tc_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   p.group_m = 16;
   p.a_bcast = g.a_bcast;
   p.bias_m = g.bias_m;
+  p.peers = g.peers;
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const int grid = int(total < dev.num_sms ? total : dev.num_sms);

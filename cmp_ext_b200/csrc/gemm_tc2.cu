@@ -48,6 +48,7 @@ struct Tc2Params {
   int* counters;  // [sk tile][rank 2][epilogue warp 4], zero on entry and exit
   int a_bcast;
   int bias_m;
+  PeerOut peers;
   int* err;
 };
 
@@ -141,7 +142,7 @@ __device__ __forceinline__ uint32_t pack2_2(float a, float b, __nv_bfloat16*) {
 // output; full 16-byte groups inside [0, N) use vector stores.
 template <typename T>
 __device__ __forceinline__ void store_row32_16(T* crow, const T* bias, float rowb, int col0, int N,
-                                               const uint32_t (&r)[32]) {
+                                               const uint32_t (&r)[32], const PeerOut& po, size_t off) {
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + rowb;
@@ -160,14 +161,18 @@ __device__ __forceinline__ void store_row32_16(T* crow, const T* bias, float row
       q.z = pack2_2(v[g * 8 + 4], v[g * 8 + 5], (T*)nullptr);
       q.w = pack2_2(v[g * 8 + 6], v[g * 8 + 7], (T*)nullptr);
       *reinterpret_cast<uint4*>(crow + c) = q;
+      for (int pi = 0; pi < po.n; ++pi) *reinterpret_cast<uint4*>(static_cast<T*>(po.base[pi]) + off + c) = q;
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         if (c + i < N) {
+          T h;
           if constexpr (std::is_same<T, __half>::value)
-            crow[c + i] = __float2half_rn(v[g * 8 + i]);
+            h = __float2half_rn(v[g * 8 + i]);
           else
-            crow[c + i] = __float2bfloat16_rn(v[g * 8 + i]);
+            h = __float2bfloat16_rn(v[g * 8 + i]);
+          crow[c + i] = h;
+          for (int pi = 0; pi < po.n; ++pi) static_cast<T*>(po.base[pi])[off + c + i] = h;
         }
     }
   }
@@ -333,7 +338,8 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int lrow = q * 32 + lane;  // row within this CTA's 128-row half
       const int row = tm * 256 + int(rank) * 128 + lrow;
-      OutT* crow = C + size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      const size_t row_off = size_t(b) * p.stride_c + size_t(row) * p.ldc;
+      OutT* crow = C + row_off;
       const OutT* colb = p.bias_m ? nullptr : bias;
       const float rowb = (p.bias_m && bias != nullptr && row < p.M) ? to_f32_2<OutT>(bias[row]) : 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PN);
@@ -355,7 +361,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
         if (whole) {
-          if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r);
+          if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r, p.peers, row_off);
         } else {
           float4* dst = reinterpret_cast<float4*>(part + c * 32);
 #pragma unroll
@@ -406,7 +412,8 @@ __global__ void __launch_bounds__(192, 1)
               uint32_t r[32];
 #pragma unroll
               for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(sum[c * 32 + i]);
-              if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + h * 128 + c * 32, p.N, r);
+              if (row < p.M)
+                store_row32_16<OutT>(crow, colb, rowb, tn * PN + h * 128 + c * 32, p.N, r, p.peers, row_off);
             }
           }
           if (lane == 0) *ctr = 0;
@@ -447,6 +454,7 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
   p.group_m = 8;
   p.a_bcast = g.a_bcast;
   p.bias_m = g.bias_m;
+  p.peers = g.peers;
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const long long pairs = dev.num_sms / 2;

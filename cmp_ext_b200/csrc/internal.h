@@ -10,6 +10,15 @@
 
 namespace cmpx {
 
+// Extra copies of C to write besides C itself: peer GPUs' buffers (mapped
+// into this process) with C's layout, so an M-sharded GEMM can deliver its
+// rows to every rank from the epilogue.  Plain stores over NVLink.
+constexpr int kMaxPeerOut = 7;
+struct PeerOut {
+  void* base[kMaxPeerOut];
+  int n;
+};
+
 // A fully resolved batched GEMM: C[b] = A[b] * op(B[b]) (+ bias), row-major.
 //   A    : [M, K] with row stride lda, batch stride sa (elements)
 //   B    : b_kmajor == 0 -> [K, N] row-major (ldb >= N)   (matmul / bmm)
@@ -28,6 +37,7 @@ struct Gemm {
   int b_kmajor;
   int a_bcast;  // batch > 1 and stride_a == 0: every batch entry uses the same A
   int bias_m;   // bias has M entries (one per row) instead of N (one per column)
+  PeerOut peers;  // also write C to these (same layout), n = 0: none
 };
 
 inline int elem_bytes(int dtype) { return dtype == CMPX_F32 ? 4 : 2; }

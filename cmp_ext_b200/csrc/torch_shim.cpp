@@ -277,7 +277,7 @@ torch::Tensor conv2d(torch::Tensor input, torch::Tensor weight, c10::optional<to
 // may be a slice of a larger tensor: row stride out.stride(0), unit column
 // stride).  Used by the M-sharded path to compute straight into its rows of
 // the gathered output.
-void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out) {
+void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vector<int64_t> peer_out = {}) {
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "matmul_into: 2-D tensors expected");
   TORCH_CHECK(a.is_cuda() && b.device() == a.device() && out.device() == a.device(), "matmul_into: one CUDA device");
   TORCH_CHECK(a.scalar_type() == b.scalar_type() && out.scalar_type() == a.scalar_type(), "Dtype mismatch");
@@ -301,6 +301,13 @@ void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out) {
   args.ldc = out.stride(0);
   args.b_layout = CMPX_B_KN;
   args.path = g_forced_path;
+  // peer_out: device addresses (in this process) of more outputs laid out
+  // like `out`, e.g. the same rows of peer GPUs' copies of the full result.
+  TORCH_CHECK(peer_out.size() <= 7, "matmul_into: at most 7 peer outputs");
+  std::vector<void*> peers(peer_out.size());
+  for (size_t i = 0; i < peer_out.size(); ++i) peers[i] = reinterpret_cast<void*>(peer_out[i]);
+  args.peer_C = peers.empty() ? nullptr : peers.data();
+  args.n_peer_C = int(peers.size());
   check_status(cmpx_gemm(&args, current_stream()), "matmul_into");
 }
 
@@ -320,8 +327,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp16_matmul", &fp16_matmul, "a[M,K] @ b[K,N] in fp16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
   m.def("bf16_matmul", &bf16_matmul, "a[M,K] @ b[K,N] in bf16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
   m.def("fp32_matmul", &fp32_matmul, "a[M,K] @ b[K,N] in fp32 (3xTF32)", py::arg("a"), py::arg("b"));
-  m.def("_matmul_into", &matmul_into, "a @ b written into out (internal)", py::arg("a"), py::arg("b"),
-        py::arg("out"));
+  m.def("_matmul_into", &matmul_into, "a @ b written into out (and peer copies of it) (internal)", py::arg("a"),
+        py::arg("b"), py::arg("out"), py::arg("peer_out") = std::vector<int64_t>{});
   m.def("_set_path", &set_path, "force a kernel path for testing: auto, tc, skinny, simt");
   m.def("_version", []() { return std::string(cmpx_version()); });
 }

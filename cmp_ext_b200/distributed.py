@@ -10,10 +10,14 @@ GEMM of the next chunk on a second stream.
 """
 from __future__ import annotations
 
+import os
 from typing import Callable
 
 import torch
 import torch.distributed as dist
+
+# Symmetric-memory outputs registered by gather_output(): data_ptr -> handle.
+_SYMM = {}
 
 
 def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
@@ -25,6 +29,21 @@ def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
     return r0, r0 + base + (1 if rank < extra else 0)
 
 
+def gather_output(M: int, N: int, dtype: torch.dtype, device, group=None) -> torch.Tensor:
+    """Allocates the full [M, N] output for ``sharded_matmul(..., gather=True,
+    transport="nvlink")``: a symmetric-memory tensor mapped into every rank
+    of `group` (a collective call; every rank passes the same shape).  The
+    buffer is reused by every call that is given it."""
+    # Only peer loads/stores are used, never NVLink multicast objects.
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+    import torch.distributed._symmetric_memory as symm_mem
+
+    t = symm_mem.empty((M, N), dtype=dtype, device=device)
+    h = symm_mem.rendezvous(t, group if group is not None else dist.group.WORLD)
+    _SYMM[t.data_ptr()] = h
+    return t
+
+
 def default_op(dtype: torch.dtype) -> Callable[[torch.Tensor, torch.Tensor], torch.Tensor]:
     import cmp_ext_b200 as cx
 
@@ -32,7 +51,8 @@ def default_op(dtype: torch.dtype) -> Callable[[torch.Tensor, torch.Tensor], tor
 
 
 def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = None, gather: bool = False,
-                   chunks: int = 1, group=None, op=None, out: torch.Tensor | None = None) -> torch.Tensor:
+                   chunks: int = 1, group=None, op=None, out: torch.Tensor | None = None,
+                   transport: str = "nccl") -> torch.Tensor:
     """This rank's rows of A @ B, or (gather=True) the full product on every rank.
 
     a_shard: this rank's rows of A, as given by ``shard_rows(M, world, rank)``.
@@ -46,6 +66,11 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
        multiplied.
     op: the per-shard GEMM (defaults to cmp_ext_b200's *_matmul for the dtype;
        tests on CPU pass torch.matmul).
+    transport: "nccl" (all-gather after the GEMM) or "nvlink": the GEMM's
+       epilogue stores every output tile to its own rows and, over NVLink, to
+       the same rows of every peer's output, overlapping the exchange with the
+       remaining tiles; one device-side barrier then completes the gather.
+       Needs `out` from gather_output() and evenly divided rows.
     """
     op_is_default = op is None
     op = op or default_op(a_shard.dtype)
@@ -73,6 +98,23 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
             out[r0:r1] = buf[r * rows: r * rows + sizes[r]]
         return out
     S = sizes[0]
+    if transport == "nvlink":
+        h = _SYMM.get(out.data_ptr())
+        if h is None or out.shape != (M, N) or not out.is_contiguous():
+            raise ValueError("transport='nvlink' needs the output from gather_output(M, N, ...)")
+        if not op_is_default:
+            raise ValueError("transport='nvlink' runs the library's own GEMM (op must be None)")
+        import cmp_ext_b200 as cx
+
+        row_bytes = N * out.element_size()
+        offset = rank * S * row_bytes
+        peers = [int(h.buffer_ptrs[p]) + offset for p in range(world) if p != rank]
+        h.barrier(channel=0)  # every rank is done with the previous contents of its output
+        cx._matmul_into(a_shard, b, out[rank * S:(rank + 1) * S], peers)
+        h.barrier(channel=0)  # every rank's stores into every output are done
+        return out
+    elif transport != "nccl":
+        raise ValueError(f"unknown transport {transport!r}")
     chunks = max(1, min(chunks, S))
     if chunks == 1:
         mine = out[rank * S:(rank + 1) * S]

@@ -90,6 +90,10 @@ typedef struct {
   size_t workspace_bytes;
   int bias_along_m;       /* 0: bias[N] added to every row; 1: bias[M] added to every column
                              (per output channel of a 1x1 convolution in NCHW) */
+  void* const* peer_C;    /* optional: n_peer_C more outputs with C's layout (strides), e.g. the same
+                             rows of C in peer GPUs' memory mapped into this process; the epilogue
+                             stores every C element to C and to each of them (tile paths only) */
+  int n_peer_C;           /* 0..7 */
 } cmpx_gemm_args;
 
 /* Replaces launch_matmul_fp16 (reference src/cuda/fp16_matmul.cu:301-340;

@@ -41,6 +41,8 @@ class GemmArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
         ("bias_along_m", ctypes.c_int),
+        ("peer_C", ctypes.POINTER(ctypes.c_void_p)),
+        ("n_peer_C", ctypes.c_int),
     ]
 
 

@@ -1,7 +1,8 @@
-"""M-sharded matmul over NCCL on two GPUs (one process per GPU, launched as
-child processes).  Skipped on a one-GPU box.  Checks that every rank ends up
-with the full product (in-place gather and chunked gather), equal to the
-product one GPU computes."""
+"""M-sharded matmul on two GPUs (one process per GPU, launched as child
+processes).  Skipped on a one-GPU box.  Checks that every rank ends up with
+the full product -- NCCL in-place gather, NCCL chunked gather, and the fused
+NVLink epilogue stores into symmetric memory -- equal to the product one GPU
+computes."""
 import os
 import socket
 import subprocess
@@ -35,6 +36,16 @@ for chunks in (1, 4):
     torch.cuda.synchronize()
     err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
     assert err <= 2 ** -7, (chunks, err)
+from cmp_ext_b200.distributed import gather_output
+out = gather_output(M, N, torch.bfloat16, "cuda")
+for rep in range(2):
+    out.fill_(float("nan"))
+    dist.barrier()
+    C = sharded_matmul(A[r0:r1].contiguous(), B, M=M, gather=True, transport="nvlink", out=out)
+    torch.cuda.synchronize()
+    assert not torch.isnan(C.float()).any(), "nvlink gather left rows unwritten"
+    err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
+    assert err <= 2 ** -7, ("nvlink", err)
 mine = sharded_matmul(A[r0:r1].contiguous(), B)
 assert torch.equal(mine, full[r0:r1]) or ((mine.float() - full[r0:r1].float()).abs().max() / full.float().abs().max()).item() <= 2 ** -7
 dist.barrier()

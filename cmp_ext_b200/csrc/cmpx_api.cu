@@ -129,6 +129,22 @@ int encode_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint6
   return r == CUDA_SUCCESS ? CMPX_OK : CMPX_ERR_CUDA;
 }
 
+// 3-D store map over C-shaped memory at `base`: {N, M, batch}, box 32 x 32,
+// no swizzle (the CTA-pair kernel's staged epilogue).
+int encode_out_map(CUtensorMap* m, const Gemm& g, void* base) {
+  const uint64_t E = uint64_t(elem_bytes(g.dtype));
+  const CUtensorMapDataType dt = g.dtype == CMPX_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t batch = g.batch < 1 ? 1 : uint64_t(g.batch);
+  const uint64_t bstride = batch > 1 ? uint64_t(g.sc) : uint64_t(g.M) * uint64_t(g.ldc);
+  cuuint64_t dims[3] = {uint64_t(g.N), uint64_t(g.M), batch};
+  cuuint64_t strides[2] = {uint64_t(g.ldc) * E, bstride * E};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CMPX_OK : CMPX_ERR_CUDA;
+}
+
 int env_forced_path() {
   static int forced = -1;
   if (forced < 0) {
@@ -343,6 +359,15 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
       st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, uint32_t(pair_n / 2))
                       : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
       if (st != CMPX_OK) return st;
+      if (g.peers.n > 0) {
+        // Output also goes to peer GPUs: staged TMA stores (bulk NVLink writes).
+        OutMaps om{};
+        om.n = 1 + g.peers.n;
+        if ((st = encode_out_map(&om.m[0], g, g.C)) != CMPX_OK) return st;
+        for (int i = 0; i < g.peers.n; ++i)
+          if ((st = encode_out_map(&om.m[1 + i], g, g.peers.base[i])) != CMPX_OK) return st;
+        return cuda_status(launch_tc2_f16(g, tA, tB, pair_n, ws, d->info, d->err_word, s, &om));
+      }
       return cuda_status(launch_tc2_f16(g, tA, tB, pair_n, ws, d->info, d->err_word, s));
     }
     st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 256)

@@ -88,7 +88,7 @@ __device__ __forceinline__ bool work_item(const Tc2Params& p, int c, int P, int 
   return true;
 }
 
-template <int FMT, bool B_KMAJOR, int PN, int STAGES_>
+template <int FMT, bool B_KMAJOR, int PN, int STAGES_, bool TMA_OUT = false>
 struct Tc2Cfg {
   static constexpr int BK = 64;                  // 128 bytes of K
   static constexpr int BH = PN / 2;              // B columns held by one CTA
@@ -98,7 +98,9 @@ struct Tc2Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int NACC = 512 / PN;          // TMEM accumulators per CTA
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 512;
+  // TMA_OUT: per epilogue warp, two 32 x 32 staging buffers (2 KB each)
+  static constexpr int STAGING_BYTES = TMA_OUT ? 4 * 2 * 2048 : 0;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + STAGING_BYTES + 1024 + 512;
   static constexpr uint32_t IDESC = make_idesc(uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, 256, PN);
   static_assert(BH % 64 == 0, "B half must be whole 64-column chunks");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
@@ -178,17 +180,41 @@ __device__ __forceinline__ void store_row32_16(T* crow, const T* bias, float row
   }
 }
 
-template <int FMT, bool B_KMAJOR, int PN, int STAGES>
+// Converts 32 accumulator columns (+ row / column bias) to packed 16-bit
+// values, 4 x 16 bytes.  Columns at or beyond N get values that are never
+// stored (TMA clips them).
+template <typename T>
+__device__ __forceinline__ void pack_row32_16(const uint32_t (&r)[32], const T* bias, float rowb, int col0, int N,
+                                              uint4 (&o)[4]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + rowb;
+  if (bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < N) v[i] += to_f32_2<T>(bias[col0 + i]);
+  }
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    o[g].x = pack2_2(v[g * 8 + 0], v[g * 8 + 1], (T*)nullptr);
+    o[g].y = pack2_2(v[g * 8 + 2], v[g * 8 + 3], (T*)nullptr);
+    o[g].z = pack2_2(v[g * 8 + 4], v[g * 8 + 5], (T*)nullptr);
+    o[g].w = pack2_2(v[g * 8 + 6], v[g * 8 + 7], (T*)nullptr);
+  }
+}
+
+template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const Tc2Params p) {
-  using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES>;
+                    const Tc2Params p, const __grid_constant__ OutMaps om) {
+  using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES, TMA_OUT>;
   using OutT = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * Cfg::STAGE_BYTES);
+  uint8_t* staging = smem + size_t(STAGES) * Cfg::STAGE_BYTES;  // TMA_OUT only
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;
   uint64_t* acc_empty = acc_full + Cfg::NACC;
@@ -321,6 +347,7 @@ __global__ void __launch_bounds__(192, 1)
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
     uint32_t lt = 0;
+    uint32_t chunk_seq = 0;  // TMA_OUT: chunks staged by this warp (buffer = parity)
     const long long P = p.sk_pairs;
     const long long first_skt =
         (p.sk_tiles > 0 && cluster_id < p.sk_pairs) ? sk_begin(cluster_id, p.sk_units, P) / num_kb : -1;
@@ -361,7 +388,27 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
         if (whole) {
-          if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r, p.peers, row_off);
+          if constexpr (TMA_OUT) {
+            // Stage the 32 x 32 chunk (row = lane, 64 B) and store it with one
+            // TMA box per destination (C, then each peer copy of it).
+            uint8_t* stg = staging + q * 4096 + (chunk_seq & 1) * 2048;
+            if (lane == 0) bulk_wait_read1();  // the store that last read this buffer is done with it
+            __syncwarp();
+            uint4 o[4];
+            pack_row32_16<OutT>(r, colb, rowb, tn * PN + c * 32, p.N, o);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stg + lane * 64 + j * 16) = o[j];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const int row0 = tm * 256 + int(rank) * 128 + q * 32;
+              for (int d = 0; d < om.n; ++d) tma_store_3d(&om.m[d], stg, tn * PN + c * 32, row0, b);
+              bulk_commit();
+            }
+            ++chunk_seq;
+          } else {
+            if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r, p.peers, row_off);
+          }
         } else {
           float4* dst = reinterpret_cast<float4*>(part + c * 32);
 #pragma unroll
@@ -422,6 +469,9 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
 
+  if constexpr (TMA_OUT) {
+    if (warp >= 2 && lane == 0) bulk_wait_all();  // staged output stores have landed
+  }
   __syncwarp();
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still signal its barriers
@@ -431,11 +481,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int FMT, bool B_KMAJOR, int PN, int STAGES>
-cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
-                            const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
-  using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES>;
-  auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES>;
+template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT>
+cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
+                           const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps& om) {
+  using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES, TMA_OUT>;
+  auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES, TMA_OUT>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
   static unsigned long long smem_set = 0;  // one flag word per kernel instantiation
   cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
@@ -485,9 +535,17 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, tA, tB, p);
+  e = cudaLaunchKernelEx(&cfg, kern, tA, tB, p, om);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+template <int FMT, bool B_KMAJOR, int PN, int STAGES>
+cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
+                            const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om) {
+  if (om != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, true>(g, tA, tB, ws, dev, dev_err, s, *om);
+  static OutMaps none{};
+  return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false>(g, tA, tB, ws, dev, dev_err, s, none);
 }
 
 }  // namespace
@@ -504,19 +562,19 @@ size_t tc2_workspace_bytes(const Gemm& g, int pair_n, const DeviceInfo& dev) {
 }
 
 cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n, void* ws,
-                           const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+                           const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om) {
   if (pair_n == 256) {
     if (g.dtype == CMPX_F16)
-      return g.b_kmajor ? launch_tc2_impl<0, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s)
-                        : launch_tc2_impl<0, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s);
-    return g.b_kmajor ? launch_tc2_impl<1, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s)
-                      : launch_tc2_impl<1, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s);
+      return g.b_kmajor ? launch_tc2_impl<0, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om)
+                        : launch_tc2_impl<0, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om);
+    return g.b_kmajor ? launch_tc2_impl<1, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om)
+                      : launch_tc2_impl<1, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om);
   }
   if (g.dtype == CMPX_F16)
-    return g.b_kmajor ? launch_tc2_impl<0, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s)
-                      : launch_tc2_impl<0, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s);
-  return g.b_kmajor ? launch_tc2_impl<1, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s)
-                    : launch_tc2_impl<1, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s);
+    return g.b_kmajor ? launch_tc2_impl<0, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om)
+                      : launch_tc2_impl<0, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om);
+  return g.b_kmajor ? launch_tc2_impl<1, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om)
+                    : launch_tc2_impl<1, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om);
 }
 
 }  // namespace cmpx

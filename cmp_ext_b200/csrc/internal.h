@@ -19,6 +19,13 @@ struct PeerOut {
   int n;
 };
 
+// TMA store maps of C and of its peer copies (box 32 x 32, no swizzle), for
+// the CTA-pair kernel's staged epilogue: m[0] = C, m[1..n-1] = peers.
+struct OutMaps {
+  CUtensorMap m[1 + kMaxPeerOut];
+  int n;
+};
+
 // A fully resolved batched GEMM: C[b] = A[b] * op(B[b]) (+ bias), row-major.
 //   A    : [M, K] with row stride lda, batch stride sa (elements)
 //   B    : b_kmajor == 0 -> [K, N] row-major (ldb >= N)   (matmul / bmm)
@@ -60,8 +67,11 @@ cudaError_t launch_tc_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMa
 // path's layout: fixed zeroed counter region first), or nullptr to run
 // whole tiles only.
 size_t tc2_workspace_bytes(const Gemm& g, int pair_n, const DeviceInfo& dev);
+// om: when non-null, the epilogue stages each 32 x 32 output chunk in shared
+// memory and writes it with TMA stores to every map in om (used when the
+// output also goes to peer GPUs: bulk writes instead of 16-byte stores).
 cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n, void* ws,
-                           const DeviceInfo& dev, int* dev_err, cudaStream_t s);
+                           const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om = nullptr);
 
 // 3xTF32 tensor-core kernel for fp32: tA/tA2 map the tf32 hi/lo splits of A,
 // tB/tB2 those of B, both packed K-major (B as [N][K]).

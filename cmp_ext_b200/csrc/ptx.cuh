@@ -258,3 +258,19 @@ __device__ __forceinline__ void mma_commit_pair_mc(uint64_t* bar, uint16_t cta_m
 }
 
 }  // namespace cmpx
+
+namespace cmpx {
+// TMA tile store (shared -> global, bulk-group completion).  Rows / columns
+// outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most one committed store group is still reading shared memory.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// Wait until every committed store group has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+}  // namespace cmpx

@@ -7,6 +7,8 @@ Pass criterion (the path's contract): for every case,
     err(build) <= err(reference kernel) + TOL
 with err = max|C - C64| / max|C64| and TOL = 1e-3 (fp16/bf16), 1e-5 (fp32).
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -235,3 +237,28 @@ def test_reference_kernel_matches_oracle(cuda, dtype, shape):
     o.ref_gpu_matmul(KIND[dtype], Ad.data_ptr(), Bd.data_ptr(), C.data_ptr(), M, N, K)
     want = o.oracle_matmul(KIND[dtype], _bits(A), _bits(B))
     assert np.array_equal(_bits(C).view(np.uint8), want.view(np.uint8))
+
+
+@pytest.mark.parametrize("path,shape", [(cabi.PATH_TC, (512, 264, 136)), (cabi.PATH_TC, (100, 264, 136)),
+                                        (cabi.PATH_SIMT, (70, 130, 33))], ids=["pair-tma", "single-cta", "simt"])
+def test_peer_outputs(cuda, path, shape):
+    """n_peer_C extra outputs receive exactly C (here two buffers on the same
+    GPU stand in for peers' memory): the CTA-pair kernel's staged TMA-store
+    epilogue, the single-CTA kernel's and the fallback's direct stores."""
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(13)
+    A = torch.randn(M, K, generator=g, device="cuda").half()
+    B = (torch.randn(K, N, generator=g, device="cuda") * 0.1).half()
+    bias = torch.randn(N, generator=g, device="cuda").half()
+    C = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+    p1 = torch.full_like(C, float("nan"))
+    p2 = torch.full_like(C, float("nan"))
+    arr = (ctypes.c_void_p * 2)(p1.data_ptr(), p2.data_ptr())
+    args = cabi.gemm_args(A, B, C, bias=bias, path=path)
+    args.peer_C = ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p))
+    args.n_peer_C = 2
+    assert cabi.gemm(args) == cabi.OK
+    torch.cuda.synchronize()
+    assert not torch.isnan(C.float()).any()
+    assert torch.equal(C, p1) and torch.equal(C, p2)
+    assert o.normwise_err(C.double().cpu().numpy(), (A.float() @ B.float() + bias.float()).double().cpu().numpy()) < 2e-3

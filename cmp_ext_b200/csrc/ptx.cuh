@@ -27,6 +27,7 @@ enum DeviceError : int {
   kDevTimeoutAccFull = 3,   // epilogue waited too long for an accumulator
   kDevTimeoutAccEmpty = 4,  // MMA waited too long for the epilogue
   kDevTimeoutFixup = 5,     // split-K reduction waited too long
+  kDevSelfTest = 6,         // cmpx_selftest_bounded_wait: the wait expired as intended
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -70,16 +71,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity.  Returns false on timeout
 // or when *abort becomes non-zero (another role of the CTA gave up).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                uint64_t timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > CMPX_WAIT_TIMEOUT_NS) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_limit(bar, parity, abort, CMPX_WAIT_TIMEOUT_NS);
 }
 
 // ---------------------------------------------------------------- TMA

@@ -169,6 +169,15 @@ CMPX_API int cmpx_matmul_skinny_noalloc(int dtype, const void* A, const void* B,
  * recorded since the last call (0 = none).  Returns CMPX_OK or CMPX_ERR_CUDA. */
 CMPX_API int cmpx_device_error(int* code);
 
+/* Diagnostic; no counterpart in the reference (which has no bounded waits).
+ * Runs one kernel whose single wait -- the bounded mbarrier wait every
+ * pipeline role of the GEMM kernels uses -- targets a barrier phase nothing
+ * completes, with a limit of `timeout_ns` (1 ns .. 10 s).  The kernel records
+ * an error code in the device error word and returns; the call synchronises
+ * `stream` and returns CMPX_ERR_DEVICE when the wait expired as intended.
+ * The device stays usable; read (and clear) the code with cmpx_device_error. */
+CMPX_API int cmpx_selftest_bounded_wait(unsigned long long timeout_ns, cmpx_stream_t stream);
+
 /* Human-readable name of a cmpx_status value. */
 CMPX_API const char* cmpx_status_string(int status);
 

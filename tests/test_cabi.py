@@ -96,3 +96,11 @@ def test_path_selection():
     assert sel(path=cabi.PATH_TC, N=250, ldb=250, ldc=250) == -1
     assert sel(dtype=cabi.F32, path=cabi.PATH_SKINNY, lda=64, ldb=256, ldc=256) == -1
     assert sel(dtype=9) == -1
+
+
+def test_selftest_rejects_bad_limits_without_device():
+    f = cabi.lib().cmpx_selftest_bounded_wait
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_ulonglong, ctypes.c_void_p]
+    assert f(0, None) == cabi.ERR_INVALID_ARG
+    assert f(20_000_000_000, None) == cabi.ERR_INVALID_ARG

@@ -249,11 +249,24 @@ int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
   // device facts (host-only path queries) assume the narrowest units.
   const int64_t sk_tiles = dev != nullptr ? skinny_tiles(g, *dev) : g.batch * ((g.N + 127) / 128);
   // (peer outputs are written by the tile kernels only)
-  const bool sk_ok = ok && g.M <= 64 && sk_tiles <= kSkinnyMaxTiles && g.peers.n == 0;
+  const bool sk_ok = ok && g.M <= 128 && sk_tiles <= kSkinnyMaxTiles && g.peers.n == 0;
   if (forced == CMPX_PATH_SKINNY) return sk_ok ? CMPX_PATH_SKINNY : -1;
   if (forced == CMPX_PATH_SIMT) return CMPX_PATH_SIMT;
   if (!ok) return CMPX_PATH_SIMT;
-  return sk_ok ? CMPX_PATH_SKINNY : CMPX_PATH_TC;
+  // M <= 64: always the skinny kernel.  64 < M <= 128: the single-CTA tile
+  // kernel runs one 128 x 256 tile per 256 columns with the whole K serial in
+  // one CTA.  When those tiles leave SMs idle and K is long next to N, the
+  // stream-K skinny kernel (MMA N = 128) splits K and wins (B200, fp16,
+  // M = 65..128: N 4096 K 14336 54 us vs 87 us; N = K = 8192 53 vs 58).  For
+  // K <= N, or few 128-column tiles (N < 2048), its split-K reduction of
+  // 128-row partials costs more than the idle SMs (N 1024 K 8192: 70 vs 48).
+  if (sk_ok && g.M <= 64) return CMPX_PATH_SKINNY;
+  if (sk_ok) {
+    const int64_t sms = dev != nullptr ? dev->num_sms : 148;
+    const int64_t tc_tiles = g.batch * ((g.N + 255) / 256);
+    if (tc_tiles < sms && g.K > g.N && g.N >= 2048) return CMPX_PATH_SKINNY;
+  }
+  return CMPX_PATH_TC;
 }
 
 // fp16/bf16 tile kernel choice: 0 = single-CTA 128x256 tiles, else CTA

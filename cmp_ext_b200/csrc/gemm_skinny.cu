@@ -1,4 +1,4 @@
-// Swap-AB, stream-K tcgen05 GEMM for skinny M (decode shapes, M <= 64).
+// Swap-AB, stream-K tcgen05 GEMM for skinny M (decode shapes, M <= 128).
 //
 // The reference runs every shape through its 128x128 SIMT tile kernel
 // (src/cuda/fp16_matmul.cu:63-283, bf16: src/cuda/bf16_matmul.cu:51-226);
@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(192, 1)
                        const SkParams p) {
   using Cfg = SkCfg<FMT, B_KMAJOR, MN, NS>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int EC = MN < 32 ? MN : 32;  // epilogue column chunk
   using T = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
 
   extern __shared__ uint8_t smem_raw[];
@@ -276,31 +277,35 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * Cfg::ACC_COLS);
 #pragma unroll 1
       for (int sub = 0; sub < NS; ++sub) {
-        float v[MN];
-#pragma unroll
-        for (int c = 0; c < MN; c += 16) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(t_row + sub * MN + c, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[c + i] = __uint_as_float(r[i]);
-        }
+        // Columns (rows of C) in chunks of EC so no MN-float array stays live.
         const int n = nt0 + sub * 128;
-        if (whole) {
-          // column n of C^T is C[:, n]: lanes write consecutive n (coalesced)
-          if (n < p.N) {
-            const float bv = (bias != nullptr && !p.bias_m) ? to_f32<T>(bias[n]) : 0.0f;
+        float* part = p.ws + (((size_t(blockIdx.x) * 2 + slot) * NS + sub) * MN) * 128;
+        const float bv = (whole && n < p.N && bias != nullptr && !p.bias_m) ? to_f32<T>(bias[n]) : 0.0f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < MN; c0 += EC) {
+          float v[EC];
 #pragma unroll
-            for (int j = 0; j < MN; ++j)
-              if (j < p.M) {
-                const float rb = (bias != nullptr && p.bias_m) ? to_f32<T>(bias[j]) : 0.0f;
-                from_f32(v[j] + bv + rb, cb + size_t(j) * p.ldc + n);
-              }
+          for (int c = 0; c < EC; c += 16) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_row + sub * MN + c0 + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[c + i] = __uint_as_float(r[i]);
           }
-        } else {
-          float* part = p.ws + (((size_t(blockIdx.x) * 2 + slot) * NS + sub) * MN) * 128;
+          if (whole) {
+            // column n of C^T is C[:, n]: lanes write consecutive n (coalesced)
+            if (n < p.N) {
 #pragma unroll
-          for (int j = 0; j < MN; ++j) __stcg(part + j * 128 + et, v[j]);
+              for (int j = 0; j < EC; ++j)
+                if (c0 + j < p.M) {
+                  const float rb = (bias != nullptr && p.bias_m) ? to_f32<T>(bias[c0 + j]) : 0.0f;
+                  from_f32(v[j] + bv + rb, cb + size_t(c0 + j) * p.ldc + n);
+                }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < EC; ++j) __stcg(part + (c0 + j) * 128 + et, v[j]);
+          }
         }
       }
       tc_fence_before();
@@ -320,25 +325,28 @@ __global__ void __launch_bounds__(192, 1)
           __threadfence();
 #pragma unroll 1
           for (int sub = 0; sub < NS; ++sub) {
-            float acc_s[MN];
-#pragma unroll
-            for (int j = 0; j < MN; ++j) acc_s[j] = 0.0f;
-            for (long long gg = g_lo; gg <= g_hi; ++gg) {
-              const long long gft = unit_begin(gg, U, G) / kbt;
-              const int sl = (tile == gft) ? 0 : 1;
-              const float* pp = p.ws + (((size_t(gg) * 2 + sl) * NS + sub) * MN) * 128;
-#pragma unroll
-              for (int j = 0; j < MN; ++j) acc_s[j] += __ldcg(pp + j * 128 + et);
-            }
             const int n = nt0 + sub * 128;
-            if (n < p.N) {
-              const float bv = (bias != nullptr && !p.bias_m) ? to_f32<T>(bias[n]) : 0.0f;
+            const float bv = (n < p.N && bias != nullptr && !p.bias_m) ? to_f32<T>(bias[n]) : 0.0f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < MN; c0 += EC) {
+              float acc_s[EC];
 #pragma unroll
-              for (int j = 0; j < MN; ++j)
-                if (j < p.M) {
-                  const float rb = (bias != nullptr && p.bias_m) ? to_f32<T>(bias[j]) : 0.0f;
-                  from_f32(acc_s[j] + bv + rb, cb + size_t(j) * p.ldc + n);
-                }
+              for (int j = 0; j < EC; ++j) acc_s[j] = 0.0f;
+              for (long long gg = g_lo; gg <= g_hi; ++gg) {
+                const long long gft = unit_begin(gg, U, G) / kbt;
+                const int sl = (tile == gft) ? 0 : 1;
+                const float* pp = p.ws + (((size_t(gg) * 2 + sl) * NS + sub) * MN + c0) * 128;
+#pragma unroll
+                for (int j = 0; j < EC; ++j) acc_s[j] += __ldcg(pp + j * 128 + et);
+              }
+              if (n < p.N) {
+#pragma unroll
+                for (int j = 0; j < EC; ++j)
+                  if (c0 + j < p.M) {
+                    const float rb = (bias != nullptr && p.bias_m) ? to_f32<T>(bias[c0 + j]) : 0.0f;
+                    from_f32(acc_s[j] + bv + rb, cb + size_t(c0 + j) * p.ldc + n);
+                  }
+              }
             }
           }
           if (lane == 0) p.counters[tile * 4 + q] = 0;
@@ -394,7 +402,9 @@ cudaError_t launch_sk_ns(const Gemm& g, const CUtensorMap& tB, const CUtensorMap
     case 8:
       if constexpr (MN <= 32) return launch_sk_impl<FMT, B_KMAJOR, MN, 8>(g, tB, tA, ws, dev, dev_err, s);
       return cudaErrorInvalidValue;
-    case 4: return launch_sk_impl<FMT, B_KMAJOR, MN, 4>(g, tB, tA, ws, dev, dev_err, s);
+    case 4:
+      if constexpr (MN <= 64) return launch_sk_impl<FMT, B_KMAJOR, MN, 4>(g, tB, tA, ws, dev, dev_err, s);
+      return cudaErrorInvalidValue;
     case 2: return launch_sk_impl<FMT, B_KMAJOR, MN, 2>(g, tB, tA, ws, dev, dev_err, s);
     default: return launch_sk_impl<FMT, B_KMAJOR, MN, 1>(g, tB, tA, ws, dev, dev_err, s);
   }
@@ -406,13 +416,14 @@ cudaError_t launch_sk_mn(const Gemm& g, const CUtensorMap& tB, const CUtensorMap
   switch (skinny_mn(g.M)) {
     case 16: return launch_sk_ns<FMT, B_KMAJOR, 16>(g, tB, tA, ws, dev, dev_err, s);
     case 32: return launch_sk_ns<FMT, B_KMAJOR, 32>(g, tB, tA, ws, dev, dev_err, s);
-    default: return launch_sk_ns<FMT, B_KMAJOR, 64>(g, tB, tA, ws, dev, dev_err, s);
+    case 64: return launch_sk_ns<FMT, B_KMAJOR, 64>(g, tB, tA, ws, dev, dev_err, s);
+    default: return launch_sk_ns<FMT, B_KMAJOR, 128>(g, tB, tA, ws, dev, dev_err, s);
   }
 }
 
 }  // namespace
 
-int skinny_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+int skinny_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)); }
 
 // Sub-slabs per work unit.  Measured on config 4 (16 x 28672 x 8192 fp16,
 // B200, 128-row k-blocks): 1 sub-slab 5221 GB/s single launch / 5657

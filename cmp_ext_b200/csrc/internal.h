@@ -84,7 +84,7 @@ cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtenso
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
                               int64_t ld, int64_t sx, bool transpose, cudaStream_t s);
 
-// Swap-AB stream-K kernel for skinny M (M <= 64), fp16/bf16.
+// Swap-AB stream-K kernel for skinny M (M <= 128), fp16/bf16.
 // tBop maps B as the MMA's 128-row operand, tAop maps A as the MMA's
 // narrow operand (box rows = mn).  ws: fp32 partials, counters: per-tile ints
 // that are zero on entry and left zero on exit.

@@ -70,7 +70,7 @@ typedef enum {
 typedef enum {
   CMPX_PATH_AUTO = 0,
   CMPX_PATH_TC = 1,     /* tcgen05 persistent tile kernel (fp16/bf16) or 3xTF32 (fp32) */
-  CMPX_PATH_SKINNY = 2, /* swap-AB stream-K tcgen05 kernel, M <= 64, fp16/bf16 */
+  CMPX_PATH_SKINNY = 2, /* swap-AB stream-K tcgen05 kernel, M <= 128, fp16/bf16 */
   CMPX_PATH_SIMT = 3    /* CUDA-core fallback */
 } cmpx_path;
 

@@ -78,10 +78,18 @@ def sel(**kw):
 
 
 def test_path_selection():
-    assert sel() == cabi.PATH_TC
+    assert sel(M=129) == cabi.PATH_TC
     assert sel(M=16) == cabi.PATH_SKINNY
     assert sel(M=64) == cabi.PATH_SKINNY
+    # 64 < M <= 128: skinny only when 256-wide tiles leave SMs idle and K > N >= 2048
     assert sel(M=65) == cabi.PATH_TC
+    assert sel() == cabi.PATH_TC
+    assert sel(M=100, N=4096, K=14336, lda=14336, ldb=4096, ldc=4096) == cabi.PATH_SKINNY
+    assert sel(M=100, N=4096, K=4096, lda=4096, ldb=4096, ldc=4096) == cabi.PATH_TC
+    assert sel(M=100, N=1024, K=8192, lda=8192, ldb=1024, ldc=1024) == cabi.PATH_TC
+    wide = 256 * 160
+    assert sel(M=128, N=wide, K=wide * 2, lda=wide * 2, ldb=wide, ldc=wide) == cabi.PATH_TC
+    assert sel(M=64, N=wide, ldb=wide, ldc=wide) == cabi.PATH_SKINNY
     assert sel(A=0x100002) == cabi.PATH_SIMT           # misaligned base
     assert sel(N=250, ldb=250, ldc=250) == cabi.PATH_SIMT  # row stride not 16-byte multiple
     assert sel(b_layout=cabi.B_NK, ldb=64) == cabi.PATH_TC
@@ -92,7 +100,8 @@ def test_path_selection():
     assert sel(dtype=cabi.F32, M=8, N=8, K=8, lda=8, ldb=8, ldc=8) == cabi.PATH_SIMT
     # forced paths
     assert sel(path=cabi.PATH_SIMT) == cabi.PATH_SIMT
-    assert sel(path=cabi.PATH_SKINNY) == -1            # M = 128 > 64
+    assert sel(path=cabi.PATH_SKINNY) == cabi.PATH_SKINNY
+    assert sel(path=cabi.PATH_SKINNY, M=129) == -1      # M > 128
     assert sel(path=cabi.PATH_TC, N=250, ldb=250, ldc=250) == -1
     assert sel(dtype=cabi.F32, path=cabi.PATH_SKINNY, lda=64, ldb=256, ldc=256) == -1
     assert sel(dtype=9) == -1

@@ -98,7 +98,8 @@ def test_tc_path_bias(cuda, b_layout):
 # ------------------------------------------------------------ skinny path
 # large-N cases: (16, 28672, 512), (16, 8192, 8192), (40, 4096, 16384)
 SK_SHAPES = [(1, 128, 64), (7, 1000, 200), (16, 4096, 1024), (17, 256, 8192), (32, 520, 640), (33, 384, 256),
-             (64, 2048, 2048), (16, 28672, 512), (16, 8192, 8192), (40, 4096, 16384)]
+             (64, 2048, 2048), (16, 28672, 512), (16, 8192, 8192), (40, 4096, 16384), (65, 640, 384),
+             (100, 4096, 2048), (128, 8192, 4096), (127, 1000, 1000)]
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])

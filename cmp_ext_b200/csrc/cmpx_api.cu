@@ -532,6 +532,17 @@ int cmpx_device_error(int* code) {
   if (v != 0) {
     const int zero = 0;
     if (cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return CMPX_ERR_CUDA;
+    // A launch that gave up may have left split-K counters or the piece
+    // claim counter non-zero: restore the library workspace's counter region
+    // (caller workspaces are the caller's to re-zero).
+    DeviceState* d = nullptr;
+    if (device_state(&d) == CMPX_OK) {
+      std::lock_guard<std::mutex> lk(d->ws_mu);
+      for (int slot = 0; slot < 2; ++slot)
+        if (d->ws[slot] != nullptr && d->ws_bytes[slot] >= kSkinnyCounterBytes &&
+            cudaMemset(d->ws[slot], 0, kSkinnyCounterBytes) != cudaSuccess)
+          return CMPX_ERR_CUDA;
+    }
   }
   *code = v;
   return CMPX_OK;

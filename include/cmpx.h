@@ -86,7 +86,8 @@ typedef struct {
   int64_t stride_a, stride_b, stride_c;  /* stride_a == 0 with batch > 1: one A shared by every batch entry */
   int b_layout;           /* cmpx_b_layout */
   int path;               /* cmpx_path (AUTO unless a test forces one) */
-  void* workspace;        /* optional caller scratch (device); NULL = library-managed */
+  void* workspace;        /* optional caller scratch (device, 16-byte aligned, zero-filled before its
+                             first use; calls leave its counters at zero); NULL = library-managed */
   size_t workspace_bytes;
   int bias_along_m;       /* 0: bias[N] added to every row; 1: bias[M] added to every column
                              (per output channel of a 1x1 convolution in NCHW) */
@@ -166,7 +167,10 @@ CMPX_API int cmpx_matmul_skinny_noalloc(int dtype, const void* A, const void* B,
 
 /* Reads and clears the device-side error word of the current device
  * (synchronises the device).  *code receives the first error a kernel
- * recorded since the last call (0 = none).  Returns CMPX_OK or CMPX_ERR_CUDA. */
+ * recorded since the last call (0 = none).  When it is non-zero, the counter
+ * region of the library-managed workspace is zeroed again (a launch that gave
+ * up can leave counters behind); a caller workspace must then be re-zeroed by
+ * the caller.  Returns CMPX_OK or CMPX_ERR_CUDA. */
 CMPX_API int cmpx_device_error(int* code);
 
 /* Diagnostic; no counterpart in the reference (which has no bounded waits).

@@ -106,3 +106,28 @@ def test_bmm_batch_beyond_grid_limit(cuda):
     b = torch.randn(70000, 8, 4, device="cuda", dtype=torch.float16)
     c = cx.bmm(a, b)
     assert _err(c, torch.bmm(a.float(), b.float())) <= TOL[torch.float16]
+
+
+@pytest.mark.parametrize("shape", [(16, 4096, 8192), (16, 28672, 8192), (8, 1024, 8192)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_skinny_in_cuda_graph(cuda, shape):
+    """The decode path (stream-K with split-K hand-offs through a
+    library workspace) captured in a CUDA graph and replayed on new inputs."""
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(3)
+    A = torch.randn(M, K, generator=g, device="cuda").half()
+    B = (torch.randn(K, N, generator=g, device="cuda") * 0.02).half()
+    first = cx.fp16_matmul(A, B)  # eager call first: workspace and kernel attributes
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        C = cx.fp16_matmul(A, B)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(C, first)
+    A.copy_(torch.randn(M, K, generator=g, device="cuda").half())
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(C, cx.fp16_matmul(A, B))
+    assert _err(C, A.float() @ B.float()) <= TOL[torch.float16]

@@ -170,9 +170,9 @@ def test_forced_path_rejections(cuda):
     run_cabi(A, B, path=cabi.PATH_TC, expect=cabi.ERR_UNSUPPORTED)
     C = run_cabi(A, B)  # auto -> SIMT
     assert torch.equal(C, torch.full_like(C, 72.0))
-    A = torch.ones((128, 64), dtype=torch.float16, device="cuda")
+    A = torch.ones((129, 64), dtype=torch.float16, device="cuda")
     B = torch.ones((64, 64), dtype=torch.float16, device="cuda")
-    run_cabi(A, B, path=cabi.PATH_SKINNY, expect=cabi.ERR_UNSUPPORTED)  # M > 64
+    run_cabi(A, B, path=cabi.PATH_SKINNY, expect=cabi.ERR_UNSUPPORTED)  # M > 128
 
 
 def test_batched_and_strided(cuda):
@@ -263,3 +263,28 @@ def test_peer_outputs(cuda, path, shape):
     assert not torch.isnan(C.float()).any()
     assert torch.equal(C, p1) and torch.equal(C, p2)
     assert o.normwise_err(C.double().cpu().numpy(), (A.float() @ B.float() + bias.float()).double().cpu().numpy()) < 2e-3
+
+
+@pytest.mark.parametrize("shape", [(16, 28672, 8192), (8, 1024, 8192), (100, 4096, 14336)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_skinny_caller_workspace(cuda, shape):
+    """Skinny path with a caller-provided (zero-filled) workspace: same bits
+    as the library-managed one, and reusable call after call."""
+    M, N, K = shape
+    g = torch.Generator().manual_seed(11)
+    A = _rand((M, K), torch.float16, g).cuda()
+    B = _rand((K, N), torch.float16, g, std=0.02).cuda()
+    ref = run_cabi(A, B, path=cabi.PATH_SKINNY)
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    args = cabi.gemm_args(A, B, C, path=cabi.PATH_SKINNY)
+    need = cabi.lib().cmpx_gemm_workspace_size(ctypes.byref(args))
+    assert need > 0
+    ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device="cuda")
+    small = cabi.gemm_args(A, B, C, path=cabi.PATH_SKINNY, workspace=ws.data_ptr(), workspace_bytes=need - 1)
+    assert cabi.gemm(small, torch.cuda.current_stream().cuda_stream) == cabi.ERR_WORKSPACE
+    for _ in range(3):
+        C.fill_(float("nan"))
+        a = cabi.gemm_args(A, B, C, path=cabi.PATH_SKINNY, workspace=ws.data_ptr(), workspace_bytes=need)
+        assert cabi.gemm(a, torch.cuda.current_stream().cuda_stream) == cabi.OK
+        torch.cuda.synchronize()
+        assert torch.equal(C, ref)

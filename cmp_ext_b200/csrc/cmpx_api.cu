@@ -438,6 +438,16 @@ int packed_matmul(int dtype, const void* A, const void* B, void* C, int64_t M, i
 
 }  // namespace
 
+// CMPX_PDL=0 turns programmatic dependent launch off (A/B measurements).
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = std::getenv("CMPX_PDL");
+    on = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 int* device_error_word() {
   DeviceState* d = nullptr;
   return device_state(&d) == CMPX_OK ? d->err_word : nullptr;

@@ -131,6 +131,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_trigger();
+  pdl_wait();
 
   const long long G = gridDim.x;
   const long long U = p.units;
@@ -391,8 +393,14 @@ cudaError_t launch_sk_impl(const Gemm& g, const CUtensorMap& tB, const CUtensorM
   p.a_bcast = g.a_bcast;
   p.bias_m = g.bias_m;
   p.err = dev_err;
-  kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(tB, tA, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  apply_pdl(cfg, attr, 0);
+  return cudaLaunchKernelEx(&cfg, kern, tB, tA, p);
 }
 
 template <int FMT, bool B_KMAJOR, int MN>

@@ -214,6 +214,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_trigger();
+  pdl_wait();
 
   const int total_tiles = p.tiles_m * p.tiles_n * p.batch;
   const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
@@ -455,8 +457,14 @@ cudaError_t launch_tc_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const int grid = int(total < dev.num_sms ? total : dev.num_sms);
-  kern<<<grid, 192, Cfg::SMEM, s>>>(tA, tB, tA2, tB2, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  apply_pdl(cfg, attr, 0);
+  return cudaLaunchKernelEx(&cfg, kern, tA, tB, tA2, tB2, p);
 }
 
 }  // namespace
@@ -500,6 +508,8 @@ __device__ __forceinline__ void split4(const float4 x, float4& h, float4& l) {
 // form: cols % 4 == 0, ld % 4 == 0 and X 16-byte aligned.
 __global__ void split_tf32_vec_kernel(const float* __restrict__ X, float* __restrict__ hi, float* __restrict__ lo,
                                       long long rows, long long cols, long long ld, long long sx) {
+  pdl_trigger();
+  pdl_wait();  // X may be the previous kernel's output
   const long long b = blockIdx.y;
   const long long c4 = cols / 4, n4 = rows * c4;
   const float* xb = X + b * sx;
@@ -517,6 +527,8 @@ __global__ void split_tf32_vec_kernel(const float* __restrict__ X, float* __rest
 
 __global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict__ hi, float* __restrict__ lo,
                                   long long rows, long long cols, long long ld, long long sx) {
+  pdl_trigger();
+  pdl_wait();  // X may be the previous kernel's output
   const long long b = blockIdx.y;
   const long long n = rows * cols;
   const float* xb = X + b * sx;
@@ -538,6 +550,8 @@ __global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float* 
                                                                    float* __restrict__ hi, float* __restrict__ lo,
                                                                    long long rows, long long cols, long long ld,
                                                                    long long sx) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float th[64][65];
   __shared__ float tl[64][65];
   const long long b = blockIdx.z;
@@ -580,6 +594,18 @@ __global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float* 
 }
 }  // namespace
 
+// 256-thread launch with the programmatic-dependent-launch attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_plain_pdl(void (*kern)(KArgs...), dim3 grid, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  apply_pdl(cfg, attr, 0);
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
                               int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
   const bool vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && cols % 4 == 0 && ld % 4 == 0 &&
@@ -589,19 +615,15 @@ cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batc
     // the tensor-core path: K (= rows) % 4 == 0 holds there.
     if (!vec || rows % 4 != 0) return cudaErrorInvalidValue;
     const dim3 grid{unsigned((cols + 63) / 64), unsigned((rows + 63) / 64), unsigned(batch)};
-    split_tf32_transpose_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
-    return cudaGetLastError();
+    return launch_plain_pdl(split_tf32_transpose_kernel, grid, s, X, hi, lo, rows, cols, ld, sx);
   }
   const long long n = vec ? rows * cols / 4 : rows * cols;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
-  if (vec)
-    split_tf32_vec_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
-  else
-    split_tf32_kernel<<<grid, 256, 0, s>>>(X, hi, lo, rows, cols, ld, sx);
-  return cudaGetLastError();
+  if (vec) return launch_plain_pdl(split_tf32_vec_kernel, grid, s, X, hi, lo, rows, cols, ld, sx);
+  return launch_plain_pdl(split_tf32_kernel, grid, s, X, hi, lo, rows, cols, ld, sx);
 }
 
 }  // namespace cmpx

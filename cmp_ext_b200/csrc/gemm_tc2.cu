@@ -245,6 +245,8 @@ __global__ void __launch_bounds__(192, 1)
   cluster_sync();  // barriers of both CTAs initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_trigger();
+  pdl_wait();
 
   const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
   const int cluster_id = blockIdx.x >> 1;
@@ -528,13 +530,12 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  apply_pdl(cfg, attr, 1);
   e = cudaLaunchKernelEx(&cfg, kern, tA, tB, p, om);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

@@ -118,6 +118,20 @@ int device_facts(DeviceInfo* info, int** err_word);
 int encode_tmap_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
                    uint64_t ld, uint64_t bstride, uint32_t box_inner, uint32_t box_rows);
 
+// Programmatic dependent launch for the GEMM kernels (on unless CMPX_PDL=0).
+bool pdl_enabled();
+// Fills `attr` (one slot) and cfg.attrs / cfg.numAttrs for a PDL launch, or
+// leaves cfg without attributes when PDL is off.
+inline void apply_pdl(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int used) {
+  cfg.attrs = attr;
+  cfg.numAttrs = used;
+  if (pdl_enabled()) {
+    attr[used].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[used].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = used + 1;
+  }
+}
+
 }  // namespace cmpx
 
 namespace cmpx {

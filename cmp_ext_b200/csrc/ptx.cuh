@@ -87,6 +87,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return mbar_wait_limit(bar, parity, abort, CMPX_WAIT_TIMEOUT_NS);
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is finishing.  Every such kernel runs its
+// prologue (barrier init, TMEM allocation), lets its own dependents launch,
+// then waits for the previous grid's completion and memory flush before it
+// reads or writes global memory.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -5,7 +5,7 @@ B [8192, 8192] ~ N(0,0.02), bf16 out -- M-sharded over the ranks (rank r owns
 rows shard_rows(16384, N, r); B replicated; no collective unless --gather).
 Total work is fixed as N grows (strong scaling).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config {2,3,4,5}]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config {2,3,4,5,6,7}]
                     [--impl ours|reference] [--gather] [--no-e2e] [--no-cpu]
 
 One step = one pass of the hot path over the resident inputs: one GEMM launch
@@ -453,7 +453,7 @@ def main(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", type=int, default=3, choices=[2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=3, choices=[2, 3, 4, 5, 6, 7])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="all-gather C to every rank (N>1)")
     ap.add_argument("--chunks", type=int, default=1, help="row chunks for the overlapped gather (1 = in place)")

@@ -38,7 +38,7 @@ struct SkParams {
   int n_tiles;    // N-tiles per batch entry
   int kbt;        // k-blocks per tile
   long long units;  // batch * n_tiles * kbt
-  float* ws;      // [grid][2][MN][128] fp32 partials
+  float* ws;      // [grid][2 slots][NS][MN/4][128 n][4] fp32 partials
   int* counters;  // [batch * n_tiles][4] (one per epilogue warp quadrant)
   int a_bcast;
   int bias_m;
@@ -305,8 +305,12 @@ __global__ void __launch_bounds__(192, 1)
                 }
             }
           } else {
+            // [MN/4][128 n][4] partials: a float4 per lane, 512 contiguous
+            // bytes per warp store
+            float4* dst = reinterpret_cast<float4*>(part) + size_t(c0 / 4) * 128 + et;
 #pragma unroll
-            for (int j = 0; j < EC; ++j) __stcg(part + (c0 + j) * 128 + et, v[j]);
+            for (int j = 0; j < EC; j += 4)
+              __stcg(dst + (j / 4) * 128, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
           }
         }
       }
@@ -325,6 +329,11 @@ __global__ void __launch_bounds__(192, 1)
         prev = __shfl_sync(0xffffffffu, prev, 0);
         if (prev == int(g_hi - g_lo)) {
           __threadfence();
+          // Only the first owner's range can start before this tile (its
+          // part then sits in that CTA's second slot); later owners start
+          // inside the tile and use their first slot.
+          const int sl_lo = unit_begin(g_lo, U, G) < tile * kbt ? 1 : 0;
+          const size_t slot_floats = size_t(NS) * MN * 128;
 #pragma unroll 1
           for (int sub = 0; sub < NS; ++sub) {
             const int n = nt0 + sub * 128;
@@ -334,12 +343,22 @@ __global__ void __launch_bounds__(192, 1)
               float acc_s[EC];
 #pragma unroll
               for (int j = 0; j < EC; ++j) acc_s[j] = 0.0f;
+              const size_t lane_off = size_t(sub) * MN * 128 + (size_t(c0 / 4) * 128 + et) * 4;
+              // parts summed in CTA order; unrolled so several parts' loads
+              // are in flight at once
+#pragma unroll 4
               for (long long gg = g_lo; gg <= g_hi; ++gg) {
-                const long long gft = unit_begin(gg, U, G) / kbt;
-                const int sl = (tile == gft) ? 0 : 1;
-                const float* pp = p.ws + (((size_t(gg) * 2 + sl) * NS + sub) * MN + c0) * 128;
+                const int sl = gg == g_lo ? sl_lo : 0;
+                const float4* pp =
+                    reinterpret_cast<const float4*>(p.ws + (size_t(gg) * 2 + sl) * slot_floats + lane_off);
 #pragma unroll
-                for (int j = 0; j < EC; ++j) acc_s[j] += __ldcg(pp + j * 128 + et);
+                for (int j = 0; j < EC; j += 4) {
+                  const float4 x = __ldcg(pp + (j / 4) * 128);
+                  acc_s[j] += x.x;
+                  acc_s[j + 1] += x.y;
+                  acc_s[j + 2] += x.z;
+                  acc_s[j + 3] += x.w;
+                }
               }
               if (n < p.N) {
 #pragma unroll

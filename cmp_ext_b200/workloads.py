@@ -8,6 +8,11 @@ Config ids follow the order of the configs list the path is judged on:
   3  bf16 M=16384 K=8192 N=8192, A ~ N(0,1), B ~ N(0,0.02)    (prefill, M-sharded)
   4  fp16 M=16 K=8192 N=28672,   A ~ N(0,1), B ~ N(0,0.02)    (decode, HBM-bound)
   5  fp32 8192^3,           A,B ~ N(0,1)                      (3xTF32)
+
+Two extra workloads carry the path's stated 1-GPU tensor target (fp16/bf16
+8192^3, >= 70% of dense peak); they are bench lines, not parity configs:
+  6  fp16 8192^3,           A,B ~ U(-1,1)
+  7  bf16 8192^3,           A ~ N(0,1), B ~ N(0,0.02)
 """
 from __future__ import annotations
 
@@ -48,6 +53,8 @@ CONFIGS = {
     3: Config(3, "bf16_matmul prefill 16384x8192x8192", torch.bfloat16, 16384, 8192, 8192, "normal", 0.02, "tensor"),
     4: Config(4, "fp16_matmul decode 16x28672x8192", torch.float16, 16, 28672, 8192, "normal", 0.02, "hbm"),
     5: Config(5, "fp32_matmul 8192^3", torch.float32, 8192, 8192, 8192, "normal", 1.0, "tensor"),
+    6: Config(6, "fp16_matmul 8192^3", torch.float16, 8192, 8192, 8192, "uniform", 1.0, "tensor"),
+    7: Config(7, "bf16_matmul 8192^3", torch.bfloat16, 8192, 8192, 8192, "normal", 0.02, "tensor"),
 }
 
 

@@ -50,7 +50,7 @@ def _errs(cfg, A, B, C, rows):
     return err, ref_err
 
 
-@pytest.mark.parametrize("cid,nrows", [(2, 256), (3, 96), (4, 16), (5, 96)])
+@pytest.mark.parametrize("cid,nrows", [(2, 256), (3, 96), (4, 16), (5, 96), (6, 128), (7, 128)])
 def test_config_within_reference_error(cuda, cid, nrows):
     cfg = CONFIGS[cid]
     A, B = make_inputs(cfg, "cpu", seed=0)

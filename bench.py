@@ -162,12 +162,19 @@ def launches_per_step(cfg, rows=None) -> int:
     return 3 if cfg.dtype == torch.float32 else 1
 
 
-def kernel_name(cfg) -> str:
+def kernel_name(cfg, m=None) -> str:
+    """The dominant kernel of a step, from the library's own path choice."""
+    from cmp_ext_b200 import _cmpext3 as ext
+
+    m = cfg.M if m is None else m
+    path = ext._matmul_path(m, cfg.N, cfg.K, cfg.dtype_name)
+    if path == "skinny":
+        return "gemm_skinny_kernel"
+    if path == "simt":
+        return "gemm_simt_kernel"
     if cfg.dtype == torch.float32:
         return "gemm_tc_kernel(3xTF32)"
-    if cfg.M <= 64:
-        return "gemm_skinny_kernel"
-    return "gemm_tc2_kernel (CTA pairs, 256x256)" if cfg.M > 128 else "gemm_tc_kernel"
+    return "gemm_tc2_kernel (CTA pairs, 256x256)" if m > 128 else "gemm_tc_kernel"
 
 
 # ------------------------------------------------------------------ CPU legs
@@ -432,7 +439,7 @@ def run_ours(args):
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": cfg.dtype_name, "data": "synthetic (seeded, drawn on device)",
                 "config": config_block(cfg, world, gather, args.transport),
-                "roofline": {"bound": rbound, "kernel": kernel_name(cfg), "achieved": achieved, "peak": peak,
+                "roofline": {"bound": rbound, "kernel": kernel_name(cfg, m), "achieved": achieved, "peak": peak,
                              "peak_source": peak_src, "unit": runit, "frac": achieved / peak,
                              "traffic": traffic, "launch_ms": avg_launch_ms, "timing": timing,
                              "isolated_launch": {"ms": launch_ms, "achieved": achieved_isolated,

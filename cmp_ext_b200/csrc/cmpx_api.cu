@@ -253,18 +253,26 @@ int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
   if (forced == CMPX_PATH_SKINNY) return sk_ok ? CMPX_PATH_SKINNY : -1;
   if (forced == CMPX_PATH_SIMT) return CMPX_PATH_SIMT;
   if (!ok) return CMPX_PATH_SIMT;
-  // M <= 64: always the skinny kernel.  64 < M <= 128: the single-CTA tile
-  // kernel runs one 128 x 256 tile per 256 columns with the whole K serial in
-  // one CTA.  When those tiles leave SMs idle and K is long next to N, the
-  // stream-K skinny kernel (MMA N = 128) splits K and wins (B200, fp16,
-  // M = 65..128: N 4096 K 14336 54 us vs 87 us; N = K = 8192 53 vs 58).  For
-  // K <= N, or few 128-column tiles (N < 2048), its split-K reduction of
-  // 128-row partials costs more than the idle SMs (N 1024 K 8192: 70 vs 48).
-  if (sk_ok && g.M <= 64) return CMPX_PATH_SKINNY;
+  // M <= 128: the single-CTA tile kernel runs one 128 x 256 tile per 256
+  // columns with the whole K serial in one CTA and no split-K reduction; the
+  // stream-K skinny kernel splits K over every SM.  Measured on a B200 (fp16,
+  // M = 1..128, 80 shapes; single launches back to back):
+  //  * T = 256-column tiles >= ~96 with K < 128 * T: the tile kernel (M 16,
+  //    N 28672, K 4096: 38.9 us vs 45.2; config 4, K 8192: 5.9-6.0 TB/s vs
+  //    5.85; N 32768 K 8192: 80 vs 91),
+  //  * fewer tiles or deeper K: the skinny kernel (N = K = 8192: 29-41 us vs
+  //    50-53; N 4096 K 14336: 26-38 vs 80-84),
+  //  * 32 < M: the skinny kernel re-reads a wider A tile per unit, so the tile
+  //    kernel also wins with fewer tiles (N 14336 K 4096, 56 tiles: 30 vs
+  //    33-46): there the skinny kernel needs K >= 128 * T,
+  //  * M < 8: the skinny kernel throughout (M 1, N 28672 K 4096: 44.6 vs 53.4).
   if (sk_ok) {
     const int64_t sms = dev != nullptr ? dev->num_sms : 148;
-    const int64_t tc_tiles = g.batch * ((g.N + 255) / 256);
-    if (tc_tiles < sms && g.K > g.N && g.N >= 2048) return CMPX_PATH_SKINNY;
+    const int64_t T = g.batch * ((g.N + 255) / 256);
+    const bool deep = g.K >= 128 * T;
+    if (g.M < 8) return CMPX_PATH_SKINNY;
+    if (g.M <= 32 && (T < 96 || T >= sms || deep)) return CMPX_PATH_SKINNY;
+    if (g.M > 32 && T < sms && deep) return CMPX_PATH_SKINNY;
   }
   return CMPX_PATH_TC;
 }

@@ -193,6 +193,31 @@ torch::Tensor matmul_2d(const torch::Tensor& a_in, const torch::Tensor& b_in, at
   return c;
 }
 
+// Kernel path cmpx_gemm picks for a packed row-major (M,K) x (K,N) matmul of
+// `dtype` ("f16", "bf16", "f32"): "tc", "skinny" or "simt".  Operand
+// addresses are taken as 256-byte aligned (as fresh torch allocations are).
+std::string matmul_path(int64_t M, int64_t N, int64_t K, const std::string& dtype) {
+  const int dt = dtype == "f32" ? CMPX_F32 : (dtype == "bf16" ? CMPX_BF16 : CMPX_F16);
+  cmpx_gemm_args a = base_args(dt);
+  a.A = reinterpret_cast<const void*>(uintptr_t(0x100000));
+  a.B = reinterpret_cast<const void*>(uintptr_t(0x200000));
+  a.C = reinterpret_cast<void*>(uintptr_t(0x300000));
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.lda = K;
+  a.ldb = N;
+  a.ldc = N;
+  a.b_layout = CMPX_B_KN;
+  a.path = g_forced_path;
+  switch (cmpx_gemm_select_path(&a)) {
+    case CMPX_PATH_TC: return "tc";
+    case CMPX_PATH_SKINNY: return "skinny";
+    case CMPX_PATH_SIMT: return "simt";
+    default: return "invalid";
+  }
+}
+
 std::vector<int64_t> pair_param(const py::object& o) {
   if (py::isinstance<py::int_>(o)) {
     const int64_t v = o.cast<int64_t>();
@@ -330,5 +355,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("_matmul_into", &matmul_into, "a @ b written into out (and peer copies of it) (internal)", py::arg("a"),
         py::arg("b"), py::arg("out"), py::arg("peer_out") = std::vector<int64_t>{});
   m.def("_set_path", &set_path, "force a kernel path for testing: auto, tc, skinny, simt");
+  m.def("_matmul_path", &matmul_path, "kernel path cmpx_gemm picks for a packed (M,K)x(K,N) matmul");
   m.def("_version", []() { return std::string(cmpx_version()); });
 }

@@ -79,17 +79,24 @@ def sel(**kw):
 
 def test_path_selection():
     assert sel(M=129) == cabi.PATH_TC
-    assert sel(M=16) == cabi.PATH_SKINNY
-    assert sel(M=64) == cabi.PATH_SKINNY
-    # 64 < M <= 128: skinny only when 256-wide tiles leave SMs idle and K > N >= 2048
-    assert sel(M=65) == cabi.PATH_TC
-    assert sel() == cabi.PATH_TC
-    assert sel(M=100, N=4096, K=14336, lda=14336, ldb=4096, ldc=4096) == cabi.PATH_SKINNY
-    assert sel(M=100, N=4096, K=4096, lda=4096, ldb=4096, ldc=4096) == cabi.PATH_TC
-    assert sel(M=100, N=1024, K=8192, lda=8192, ldb=1024, ldc=1024) == cabi.PATH_TC
+    assert sel(M=16) == cabi.PATH_SKINNY                   # one tile, K 64
+    kw = lambda M, N, K: dict(M=M, N=N, K=K, lda=K, ldb=N, ldc=N)
+    # M <= 32: skinny unless ~96+ tiles of 256 columns with K < 128 * tiles
+    assert sel(**kw(16, 28672, 8192)) == cabi.PATH_TC       # config 4: 112 tiles
+    assert sel(**kw(16, 14336, 4096)) == cabi.PATH_SKINNY   # 56 tiles
+    assert sel(**kw(32, 16384, 16384)) == cabi.PATH_SKINNY  # 64 tiles
+    assert sel(**kw(4, 28672, 8192)) == cabi.PATH_SKINNY    # M < 8: always skinny
+    # 32 < M <= 128: skinny when K >= 128 * tiles and the tiles leave SMs idle
+    assert sel(M=64) == cabi.PATH_TC                       # N 256, K 64: one shallow tile
+    assert sel(**kw(65, 4096, 4096)) == cabi.PATH_SKINNY
+    assert sel(**kw(100, 4096, 14336)) == cabi.PATH_SKINNY
+    assert sel(**kw(128, 8192, 8192)) == cabi.PATH_SKINNY
+    assert sel(**kw(100, 8192, 2048)) == cabi.PATH_TC
+    assert sel(**kw(48, 14336, 4096)) == cabi.PATH_TC
+    assert sel(**kw(64, 28672, 4096)) == cabi.PATH_TC
+    assert sel(**kw(128, 1024, 8192)) == cabi.PATH_SKINNY
     wide = 256 * 160
-    assert sel(M=128, N=wide, K=wide * 2, lda=wide * 2, ldb=wide, ldc=wide) == cabi.PATH_TC
-    assert sel(M=64, N=wide, ldb=wide, ldc=wide) == cabi.PATH_SKINNY
+    assert sel(**kw(128, wide, wide * 2)) == cabi.PATH_TC
     assert sel(A=0x100002) == cabi.PATH_SIMT           # misaligned base
     assert sel(N=250, ldb=250, ldc=250) == cabi.PATH_SIMT  # row stride not 16-byte multiple
     assert sel(b_layout=cabi.B_NK, ldb=64) == cabi.PATH_TC

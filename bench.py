@@ -157,8 +157,9 @@ def op_for(dtype):
 
 def launches_per_step(cfg, rows=None) -> int:
     """Kernels of this library one step launches (per rank): the GEMM, plus
-    the two tf32 split pre-passes on the fp32 tensor-core path (fp32 with
-    K % 4 == 0 and more than 2^22 multiply-adds, as all fp32 configs here)."""
+    the two split pre-passes (tf32 or bf16 hi/lo) on the fp32 tensor-core
+    paths (fp32 with K % 4 == 0 and more than 2^22 multiply-adds, as all fp32
+    configs here)."""
     return 3 if cfg.dtype == torch.float32 else 1
 
 
@@ -172,6 +173,8 @@ def kernel_name(cfg, m=None) -> str:
         return "gemm_skinny_kernel"
     if path == "simt":
         return "gemm_simt_kernel"
+    if path == "bf16x3":
+        return "gemm_tc_kernel(bf16x3)"
     if cfg.dtype == torch.float32:
         return "gemm_tc_kernel(3xTF32)"
     return "gemm_tc2_kernel (CTA pairs, 256x256)" if m > 128 else "gemm_tc_kernel"
@@ -279,6 +282,10 @@ def run_ours(args):
     if args.quick:
         args.no_e2e = args.no_cpu = True
     op = op_for(cfg.dtype)
+    if cfg.dtype == torch.float32 and args.f32_path == "bf16x3":
+        from cmp_ext_b200 import _cmpext3 as ext
+
+        ext._set_path("bf16x3")  # every fp32 call of this process, e2e included
 
     # Inputs resident in HBM (drawn on the device, seeded per config).
     A, B = make_inputs(cfg, device, seed=0, m=m)
@@ -445,7 +452,8 @@ def run_ours(args):
         line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": cfg.dtype_name, "data": "synthetic (seeded, drawn on device)",
-                "config": config_block(cfg, world, gather, args.transport),
+                "config": {**config_block(cfg, world, gather, args.transport),
+                           **({"f32_path": args.f32_path} if cfg.dtype == torch.float32 else {})},
                 "roofline": {"bound": rbound, "kernel": kernel_name(cfg, m), "achieved": achieved, "peak": peak,
                              "peak_source": peak_src, "unit": runit, "frac": achieved / peak,
                              "traffic": traffic, "launch_ms": avg_launch_ms, "timing": timing,
@@ -479,6 +487,8 @@ def main(argv=None):
     ap.add_argument("--quick", action="store_true",
                     help="profiling mode: only W warm-up + K timed steps (no clock sampling, e2e or CPU legs)")
     ap.add_argument("--rows", type=int, default=None, help="override this rank's M rows (profiling small cases)")
+    ap.add_argument("--f32-path", default="tf32x3", choices=["tf32x3", "bf16x3"],
+                    help="fp32 configs: 3xTF32 (default) or the opt-in bf16x3 split")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)

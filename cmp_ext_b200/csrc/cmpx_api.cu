@@ -154,6 +154,7 @@ int env_forced_path() {
       if (!std::strcmp(e, "tc")) forced = CMPX_PATH_TC;
       else if (!std::strcmp(e, "skinny")) forced = CMPX_PATH_SKINNY;
       else if (!std::strcmp(e, "simt")) forced = CMPX_PATH_SIMT;
+      else if (!std::strcmp(e, "bf16x3")) forced = CMPX_PATH_BF16X3;
     }
   }
   return forced;
@@ -163,7 +164,7 @@ int validate(const cmpx_gemm_args* a) {
   if (a == nullptr) return CMPX_ERR_INVALID_ARG;
   if (a->dtype != CMPX_F16 && a->dtype != CMPX_BF16 && a->dtype != CMPX_F32) return CMPX_ERR_INVALID_ARG;
   if (a->b_layout != CMPX_B_KN && a->b_layout != CMPX_B_NK) return CMPX_ERR_INVALID_ARG;
-  if (a->path < CMPX_PATH_AUTO || a->path > CMPX_PATH_SIMT) return CMPX_ERR_INVALID_ARG;
+  if (a->path < CMPX_PATH_AUTO || a->path > CMPX_PATH_BF16X3) return CMPX_ERR_INVALID_ARG;
   if (a->batch < 0 || a->M < 0 || a->N < 0 || a->K < 0) return CMPX_ERR_INVALID_ARG;
   const int64_t lim = (int64_t(1) << 31) - 1;
   if (a->M > lim || a->N > lim || a->K > lim) return CMPX_ERR_UNSUPPORTED;
@@ -232,6 +233,10 @@ bool tma_ok_f32(const Gemm& g) {
   return a_ok && b_ok && c_ok;
 }
 
+// fp32 bf16x3: the same re-packing with 2-byte elements, so the packed row
+// length K must be a multiple of 8.
+bool tma_ok_bf16x3(const Gemm& g) { return g.K % 8 == 0 && tma_ok_f32(g); }
+
 int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
   int forced = requested != CMPX_PATH_AUTO ? requested : env_forced_path();
   if (g.K == 0) return CMPX_PATH_SIMT;  // fill kernel
@@ -239,11 +244,16 @@ int choose_path(const Gemm& g, int requested, const DeviceInfo* dev) {
     const bool ok = tma_ok_f32(g);
     if (forced == CMPX_PATH_SKINNY) return -1;
     if (forced == CMPX_PATH_TC) return ok ? CMPX_PATH_TC : -1;
+    if (forced == CMPX_PATH_BF16X3) return tma_ok_bf16x3(g) ? CMPX_PATH_BF16X3 : -1;
     if (forced == CMPX_PATH_SIMT) return CMPX_PATH_SIMT;
     const double work = double(g.batch) * double(g.M) * double(g.N) * double(g.K);
     return (ok && work >= double(1 << 22)) ? CMPX_PATH_TC : CMPX_PATH_SIMT;
   }
   const bool ok = tma_ok_16bit(g);
+  if (forced == CMPX_PATH_BF16X3) {
+    if (requested == CMPX_PATH_BF16X3) return -1;  // an fp32-only path
+    forced = CMPX_PATH_AUTO;                       // the environment switch concerns fp32 only
+  }
   if (forced == CMPX_PATH_TC) return ok ? CMPX_PATH_TC : -1;
   // The skinny path's counter region holds kSkinnyMaxTiles tiles; without
   // device facts (host-only path queries) assume the narrowest units.
@@ -315,16 +325,18 @@ bool tc_streamk(const Gemm& g) {
   return forced == 1;
 }
 
-size_t f32_split_bytes(const Gemm& g) {
+// hi and lo splits of A and B, elem bytes each (4: tf32, 2: bf16).
+size_t f32_split_bytes(const Gemm& g, size_t elem) {
   const size_t a = size_t(g.batch) * size_t(g.M) * size_t(g.K);
   const size_t b = size_t(g.batch) * size_t(g.K) * size_t(g.N);
-  auto up = [](size_t x) { return (x * 4 + 255) / 256 * 256; };
+  auto up = [elem](size_t x) { return (x * elem + 255) / 256 * 256; };
   return 2 * up(a) + 2 * up(b);
 }
 
 size_t workspace_for(const Gemm& g, int path, const DeviceInfo& dev) {
   if (path == CMPX_PATH_SKINNY) return skinny_workspace_bytes(g, dev);
-  if (path == CMPX_PATH_TC && g.dtype == CMPX_F32) return f32_split_bytes(g);
+  if (path == CMPX_PATH_TC && g.dtype == CMPX_F32) return f32_split_bytes(g, 4);
+  if (path == CMPX_PATH_BF16X3) return f32_split_bytes(g, 2);
   if (path == CMPX_PATH_TC) {
     const int pair_n = tc_pair_n(g, dev);
     return (pair_n > 0 && tc_streamk(g)) ? tc2_workspace_bytes(g, pair_n, dev) : 0;
@@ -397,31 +409,45 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
     return cuda_status(launch_tc_f16(g, tA, tB, 256, d->info, d->err_word, s));
   }
 
-  // fp32: split A and B into packed tf32 hi/lo, then 3xTF32 on the tensor
-  // cores.  B is always stored K-major ([N][K]) by the pre-pass: a [K,N]
-  // source is transposed while it is split.
+  // fp32: split A and B into packed hi/lo operands (tf32 for 3xTF32, bf16
+  // for bf16x3), then three products per k on the tensor cores.  B is always
+  // stored K-major ([N][K]) by the pre-pass: a [K,N] source is transposed
+  // while it is split.
+  const bool bf = path == CMPX_PATH_BF16X3;
+  const size_t elem = bf ? 2 : 4;
   const size_t a_elems = size_t(g.batch) * size_t(g.M) * size_t(g.K);
   const size_t b_elems = size_t(g.batch) * size_t(g.K) * size_t(g.N);
-  auto up = [](size_t x) { return (x * 4 + 255) / 256 * 256; };
+  auto up = [elem](size_t x) { return (x * elem + 255) / 256 * 256; };
   uint8_t* base = reinterpret_cast<uint8_t*>(ws);
-  float* a_hi = reinterpret_cast<float*>(base);
-  float* a_lo = reinterpret_cast<float*>(base + up(a_elems));
-  float* b_hi = reinterpret_cast<float*>(base + 2 * up(a_elems));
-  float* b_lo = reinterpret_cast<float*>(base + 2 * up(a_elems) + up(b_elems));
+  void* a_hi = base;
+  void* a_lo = base + up(a_elems);
+  void* b_hi = base + 2 * up(a_elems);
+  void* b_lo = base + 2 * up(a_elems) + up(b_elems);
   const int64_t a_batch = g.a_bcast ? 1 : g.batch;  // a shared A is split once
-  cudaError_t e = launch_split_tf32(reinterpret_cast<const float*>(g.A), a_hi, a_lo, a_batch, g.M, g.K, g.lda, g.sa,
-                                    false, s);
-  if (e != cudaSuccess) return CMPX_ERR_CUDA;
   const int64_t b_rows = g.b_kmajor ? g.N : g.K, b_cols = g.b_kmajor ? g.K : g.N;
-  e = launch_split_tf32(reinterpret_cast<const float*>(g.B), b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb,
-                        !g.b_kmajor, s);
+  const float* fA = reinterpret_cast<const float*>(g.A);
+  const float* fB = reinterpret_cast<const float*>(g.B);
+  cudaError_t e;
+  if (bf) {
+    e = launch_split_bf16(fA, a_hi, a_lo, a_batch, g.M, g.K, g.lda, g.sa, false, s);
+    if (e == cudaSuccess) e = launch_split_bf16(fB, b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb, !g.b_kmajor, s);
+  } else {
+    e = launch_split_tf32(fA, static_cast<float*>(a_hi), static_cast<float*>(a_lo), a_batch, g.M, g.K, g.lda, g.sa,
+                          false, s);
+    if (e == cudaSuccess)
+      e = launch_split_tf32(fB, static_cast<float*>(b_hi), static_cast<float*>(b_lo), g.batch, b_rows, b_cols, g.ldb,
+                            g.sb, !g.b_kmajor, s);
+  }
   if (e != cudaSuccess) return CMPX_ERR_CUDA;
   CUtensorMap tA, tA2, tB, tB2;
   const uint64_t sa = uint64_t(g.M) * uint64_t(g.K), sb = uint64_t(g.N) * uint64_t(g.K);
-  if ((st = encode_3d(&tA, CMPX_F32, a_hi, g.K, g.M, a_batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
-  if ((st = encode_3d(&tA2, CMPX_F32, a_lo, g.K, g.M, a_batch, g.K, sa, 32, 128)) != CMPX_OK) return st;
-  if ((st = encode_3d(&tB, CMPX_F32, b_hi, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
-  if ((st = encode_3d(&tB2, CMPX_F32, b_lo, g.K, g.N, g.batch, g.K, sb, 32, 128)) != CMPX_OK) return st;
+  const int op = bf ? CMPX_BF16 : CMPX_F32;     // element type of the packed operands
+  const uint32_t box_k = bf ? 64 : 32;          // one 128-byte swizzle row of K
+  if ((st = encode_3d(&tA, op, a_hi, g.K, g.M, a_batch, g.K, sa, box_k, 128)) != CMPX_OK) return st;
+  if ((st = encode_3d(&tA2, op, a_lo, g.K, g.M, a_batch, g.K, sa, box_k, 128)) != CMPX_OK) return st;
+  if ((st = encode_3d(&tB, op, b_hi, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
+  if ((st = encode_3d(&tB2, op, b_lo, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
+  if (bf) return cuda_status(launch_tc_bf16x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));
   return cuda_status(launch_tc_tf32x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));
 }
 

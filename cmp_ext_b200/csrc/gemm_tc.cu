@@ -42,15 +42,17 @@ struct TcParams {
   int* err;
 };
 
-// FMT: 0 = f16, 1 = bf16, 2 = tf32x3 (fp32 in/out)
+// FMT: 0 = f16, 1 = bf16, 2 = tf32x3 (fp32 in/out, tf32 hi/lo operands),
+//      3 = bf16x3 (fp32 in/out, bf16 hi/lo operands)
 template <int FMT, bool B_KMAJOR, int BN_, int STAGES_>
 struct TcCfg {
-  static constexpr int E = FMT == 2 ? 4 : 2;  // input/output element bytes
+  static constexpr bool SPLIT = FMT >= 2;     // fp32 product from hi/lo operand splits
+  static constexpr int E = FMT == 2 ? 4 : 2;  // operand element bytes in shared memory
   static constexpr int BM = 128;
   static constexpr int BN = BN_;
   static constexpr int STAGES = STAGES_;
   static constexpr int BK = 128 / E;         // one 128-byte swizzle atom of K
-  static constexpr int NOPS = FMT == 2 ? 2 : 1;  // hi (+ lo) copies per operand
+  static constexpr int NOPS = SPLIT ? 2 : 1;  // hi (+ lo) copies per operand
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
@@ -58,21 +60,23 @@ struct TcCfg {
   static constexpr int CHUNK_BYTES = BK * 128;
   static constexpr int KSTEP_BYTES_MN = (32 / E) * 128;  // UMMA_K rows of an MN-major tile
   // TMEM accumulator buffers.  fp16/bf16: two (epilogue of tile i overlaps
-  // the main loop of tile i+1), one per tile.  3xTF32: the tensor core's fp32
-  // accumulation over long MMA chains drifts (its rounding is biased), so the
-  // K loop is cut into chunks of KCH k-blocks, each summed afresh in TMEM and
-  // added into fp32 registers by the epilogue with IEEE round-to-nearest;
-  // four buffers let the MMA run three chunks ahead.
-  static constexpr int NACC = FMT == 2 ? 4 : 2;
-  static constexpr int KCH = FMT == 2 ? 4 : (1 << 30);
+  // the main loop of tile i+1), one per tile.  Split formats: the tensor
+  // core's fp32 accumulation over long MMA chains drifts (its rounding is
+  // biased), so the K loop is cut into chunks of KCH k-blocks (128 elements of
+  // K), each summed afresh in TMEM and added into fp32 registers by the
+  // epilogue with IEEE round-to-nearest; four buffers let the MMA run three
+  // chunks ahead.
+  static constexpr int NACC = SPLIT ? 4 : 2;
+  static constexpr int KCH = SPLIT ? 128 / BK : (1 << 30);
   static constexpr uint32_t TMEM_COLS = NACC * BN;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 512;
-  static constexpr uint32_t IDESC = make_idesc(FMT == 2 ? 2u : uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, BM, BN);
+  // operand formats: 0 = f16, 1 = bf16 (kind::f16), 2 = tf32 (kind::tf32)
+  static constexpr uint32_t IDESC = make_idesc(FMT == 2 ? 2u : FMT == 0 ? 0u : 1u, 0u, B_KMAJOR ? 0u : 1u, BM, BN);
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert(B_KMAJOR || BN % CW == 0, "BN must be whole N-major chunks");
   // An MN-major tf32 operand needs the 128B swizzle with 32B atoms; the
   // split pre-pass stores fp32 B K-major instead, so that form is not built.
-  static_assert(FMT != 2 || B_KMAJOR, "3xTF32 takes B K-major");
+  static_assert(!SPLIT || B_KMAJOR, "the split formats take B K-major");
 };
 
 __device__ __forceinline__ void decode_tile(int t, const TcParams& p, int& b, int& tm, int& tn) {
@@ -179,7 +183,7 @@ __global__ void __launch_bounds__(192, 1)
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const TcParams p) {
   using Cfg = TcCfg<FMT, B_KMAJOR, BN, STAGES>;
-  using OutT = typename std::conditional<FMT == 0, __half, typename std::conditional<FMT == 1, __nv_bfloat16, float>::type>::type;
+  using OutT = typename std::conditional<FMT == 0, __half, typename std::conditional<FMT == 1, __nv_bfloat16, float>::type>::type;  // split formats: fp32
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
@@ -225,7 +229,7 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       prefetch_tmap(&tmA);
       prefetch_tmap(&tmB);
-      if (FMT == 2) {
+      if (Cfg::SPLIT) {
         prefetch_tmap(&tmA2);
         prefetch_tmap(&tmB2);
       }
@@ -248,15 +252,15 @@ __global__ void __launch_bounds__(192, 1)
           const int k0 = kb * Cfg::BK;
           const int za = p.a_bcast ? 0 : b;
           tma_load_3d(sA, &tmA, &full_bar[stage], k0, m0, za);
-          if (FMT == 2) tma_load_3d(sA + Cfg::A_BYTES, &tmA2, &full_bar[stage], k0, m0, za);
+          if (Cfg::SPLIT) tma_load_3d(sA + Cfg::A_BYTES, &tmA2, &full_bar[stage], k0, m0, za);
           if (B_KMAJOR) {
             tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0, b);
-            if (FMT == 2) tma_load_3d(sB + Cfg::B_BYTES, &tmB2, &full_bar[stage], k0, n0, b);
+            if (Cfg::SPLIT) tma_load_3d(sB + Cfg::B_BYTES, &tmB2, &full_bar[stage], k0, n0, b);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / Cfg::CW; ++j) {
               tma_load_3d(sB + j * Cfg::CHUNK_BYTES, &tmB, &full_bar[stage], n0 + j * Cfg::CW, k0, b);
-              if (FMT == 2)
+              if (Cfg::SPLIT)
                 tma_load_3d(sB + Cfg::B_BYTES + j * Cfg::CHUNK_BYTES, &tmB2, &full_bar[stage], n0 + j * Cfg::CW,
                             k0, b);
             }
@@ -318,13 +322,19 @@ __global__ void __launch_bounds__(192, 1)
                                               : make_sdesc_sw128(b_addr + ks * Cfg::KSTEP_BYTES_MN,
                                                                  Cfg::CHUNK_BYTES, 1024);
               const uint32_t accum = (kb != kc || ks != 0) ? 1u : 0u;
-              if constexpr (FMT == 2) {
+              if constexpr (Cfg::SPLIT) {
                 const uint64_t adesc_lo = make_sdesc_sw128(a_addr + Cfg::A_BYTES + ks * 32, 16, 1024);
                 const uint64_t bdesc_lo = make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * 32, 16, 1024);
                 // small cross terms first, then the dominant hi*hi product
-                mma_tf32(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
-                mma_tf32(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
-                mma_tf32(d_tmem, adesc, bdesc, Cfg::IDESC, 1u);
+                if constexpr (FMT == 2) {
+                  mma_tf32(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
+                  mma_tf32(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
+                  mma_tf32(d_tmem, adesc, bdesc, Cfg::IDESC, 1u);
+                } else {
+                  mma_f16(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
+                  mma_f16(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
+                  mma_f16(d_tmem, adesc, bdesc, Cfg::IDESC, 1u);
+                }
               } else {
                 mma_f16(d_tmem, adesc, bdesc, Cfg::IDESC, accum);
               }
@@ -360,7 +370,7 @@ __global__ void __launch_bounds__(192, 1)
       OutT* crow = C + row_off;
       const OutT* colb = p.bias_m ? nullptr : bias;
       const float rowb = (p.bias_m && bias != nullptr && row < p.M) ? to_f32<OutT>(bias[row]) : 0.0f;
-      if constexpr (FMT == 2) {
+      if constexpr (Cfg::SPLIT) {
         // Sum the tile's chunks in registers (IEEE fp32 adds), then store.
         float racc[BN];
 #pragma unroll
@@ -485,7 +495,16 @@ cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtenso
   return launch_tc_impl<2, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
 }
 
+cudaError_t launch_tc_bf16x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
+                             const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  return launch_tc_impl<3, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
+}
+
 // ------------------------------------------------------------------ split
+// fp32 X -> hi + lo with hi = round(x), lo = round(x - hi), in one of two
+// operand formats: tf32 (kept in fp32 containers, cvt.rna) for 3xTF32, or
+// bf16 (round-to-nearest-even) for bf16x3.  hi*hi + hi*lo + lo*hi then
+// recovers the product to about 2^-21 (tf32) or 2^-16 (bf16) relative.
 namespace {
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
@@ -493,71 +512,95 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
-__device__ __forceinline__ void split4(const float4 x, float4& h, float4& l) {
-  h.x = tf32_rna(x.x);
-  h.y = tf32_rna(x.y);
-  h.z = tf32_rna(x.z);
-  h.w = tf32_rna(x.w);
-  l.x = tf32_rna(x.x - h.x);
-  l.y = tf32_rna(x.y - h.y);
-  l.z = tf32_rna(x.z - h.z);
-  l.w = tf32_rna(x.w - h.w);
+__device__ __forceinline__ void split1(float x, float& h, float& l) {
+  h = tf32_rna(x);
+  l = tf32_rna(x - h);
 }
+__device__ __forceinline__ void split1(float x, __nv_bfloat16& h, __nv_bfloat16& l) {
+  h = __float2bfloat16_rn(x);
+  l = __float2bfloat16_rn(x - __bfloat162float(h));
+}
+
+// Four consecutive split values as one 16-byte (tf32) or 8-byte (bf16) store.
+template <typename S>
+struct Vec4;
+template <>
+struct Vec4<float> {
+  float4 v;
+  __device__ __forceinline__ void set(int i, float x) { (&v.x)[i] = x; }
+  __device__ __forceinline__ void store(float* p) const { __stcs(reinterpret_cast<float4*>(p), v); }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  __nv_bfloat16 v[4];
+  __device__ __forceinline__ void set(int i, __nv_bfloat16 x) { v[i] = x; }
+  __device__ __forceinline__ void store(__nv_bfloat16* p) const {
+    uint2 u;
+    u.x = uint32_t(__bfloat16_as_ushort(v[0])) | (uint32_t(__bfloat16_as_ushort(v[1])) << 16);
+    u.y = uint32_t(__bfloat16_as_ushort(v[2])) | (uint32_t(__bfloat16_as_ushort(v[3])) << 16);
+    __stcs(reinterpret_cast<uint2*>(p), u);
+  }
+};
 
 // X [rows][cols] (row stride ld) -> packed hi, lo [rows][cols].  Vector
 // form: cols % 4 == 0, ld % 4 == 0 and X 16-byte aligned.
-__global__ void split_tf32_vec_kernel(const float* __restrict__ X, float* __restrict__ hi, float* __restrict__ lo,
-                                      long long rows, long long cols, long long ld, long long sx) {
+template <typename S>
+__global__ void split_vec_kernel(const float* __restrict__ X, S* __restrict__ hi, S* __restrict__ lo,
+                                 long long rows, long long cols, long long ld, long long sx) {
   pdl_trigger();
   pdl_wait();  // X may be the previous kernel's output
   const long long b = blockIdx.y;
   const long long c4 = cols / 4, n4 = rows * c4;
   const float* xb = X + b * sx;
-  float4* hb = reinterpret_cast<float4*>(hi + b * rows * cols);
-  float4* lb = reinterpret_cast<float4*>(lo + b * rows * cols);
+  S* hb = hi + b * rows * cols;
+  S* lb = lo + b * rows * cols;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / c4, c = i - r * c4;
     const float4 x = __ldcs(reinterpret_cast<const float4*>(xb + r * ld) + c);
-    float4 h, l;
-    split4(x, h, l);
-    __stcs(hb + i, h);
-    __stcs(lb + i, l);
+    Vec4<S> h, l;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      S hj, lj;
+      split1((&x.x)[j], hj, lj);
+      h.set(j, hj);
+      l.set(j, lj);
+    }
+    h.store(hb + 4 * i);
+    l.store(lb + 4 * i);
   }
 }
 
-__global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict__ hi, float* __restrict__ lo,
-                                  long long rows, long long cols, long long ld, long long sx) {
+template <typename S>
+__global__ void split_kernel(const float* __restrict__ X, S* __restrict__ hi, S* __restrict__ lo, long long rows,
+                             long long cols, long long ld, long long sx) {
   pdl_trigger();
   pdl_wait();  // X may be the previous kernel's output
   const long long b = blockIdx.y;
   const long long n = rows * cols;
   const float* xb = X + b * sx;
-  float* hb = hi + b * n;
-  float* lb = lo + b * n;
+  S* hb = hi + b * n;
+  S* lb = lo + b * n;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / cols, c = i - r * cols;
-    const float x = xb[r * ld + c];
-    const float h = tf32_rna(x);
-    hb[i] = h;
-    lb[i] = tf32_rna(x - h);
+    split1(xb[r * ld + c], hb[i], lb[i]);
   }
 }
 
 // Same split, writing the transpose ([cols][rows]) through 64x64 shared
-// tiles; float4 reads along cols and float4 writes along rows (vector form:
-// rows % 4 == 0, cols % 4 == 0, ld % 4 == 0, X 16-byte aligned).
-__global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float* __restrict__ X,
-                                                                   float* __restrict__ hi, float* __restrict__ lo,
-                                                                   long long rows, long long cols, long long ld,
-                                                                   long long sx) {
+// tiles; float4 reads along cols and 4-element vector writes along rows
+// (vector form: rows % 4 == 0, cols % 4 == 0, ld % 4 == 0, X 16-byte aligned).
+template <typename S>
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ X, S* __restrict__ hi,
+                                                              S* __restrict__ lo, long long rows, long long cols,
+                                                              long long ld, long long sx) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float th[64][65];
-  __shared__ float tl[64][65];
+  __shared__ S th[64][65];
+  __shared__ S tl[64][65];
   const long long b = blockIdx.z;
   const float* xb = X + b * sx;
-  float* hb = hi + b * rows * cols;
-  float* lb = lo + b * rows * cols;
+  S* hb = hi + b * rows * cols;
+  S* lb = lo + b * rows * cols;
   const long long r0 = (long long)blockIdx.y * 64, c0 = (long long)blockIdx.x * 64;
   const int t = threadIdx.x;
 #pragma unroll
@@ -567,28 +610,24 @@ __global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float* 
     const long long r = r0 + rr, c = c0 + cc;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r < rows && c < cols) x = __ldcs(reinterpret_cast<const float4*>(xb + r * ld + c));
-    float4 h, l;
-    split4(x, h, l);
-    th[rr][cc] = h.x;
-    th[rr][cc + 1] = h.y;
-    th[rr][cc + 2] = h.z;
-    th[rr][cc + 3] = h.w;
-    tl[rr][cc] = l.x;
-    tl[rr][cc + 1] = l.y;
-    tl[rr][cc + 2] = l.z;
-    tl[rr][cc + 3] = l.w;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) split1((&x.x)[j], th[rr][cc + j], tl[rr][cc + j]);
   }
   __syncthreads();
 #pragma unroll
-  for (int it = 0; it < 4; ++it) {  // 64 output rows (= input cols) x 16 float4 along input rows
+  for (int it = 0; it < 4; ++it) {  // 64 output rows (= input cols) x 16 vectors along input rows
     const int e = t + it * 256;
     const int cc = e >> 4, rr = (e & 15) * 4;
     const long long c = c0 + cc, r = r0 + rr;
     if (c < cols && r < rows) {
-      __stcs(reinterpret_cast<float4*>(hb + c * rows + r),
-             make_float4(th[rr][cc], th[rr + 1][cc], th[rr + 2][cc], th[rr + 3][cc]));
-      __stcs(reinterpret_cast<float4*>(lb + c * rows + r),
-             make_float4(tl[rr][cc], tl[rr + 1][cc], tl[rr + 2][cc], tl[rr + 3][cc]));
+      Vec4<S> h, l;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        h.set(j, th[rr + j][cc]);
+        l.set(j, tl[rr + j][cc]);
+      }
+      h.store(hb + c * rows + r);
+      l.store(lb + c * rows + r);
     }
   }
 }
@@ -606,8 +645,10 @@ cudaError_t launch_plain_pdl(void (*kern)(KArgs...), dim3 grid, cudaStream_t s, 
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
-cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
-                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
+namespace {
+template <typename S>
+cudaError_t launch_split_impl(const float* X, S* hi, S* lo, int64_t batch, int64_t rows, int64_t cols, int64_t ld,
+                              int64_t sx, bool transpose, cudaStream_t s) {
   const bool vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && cols % 4 == 0 && ld % 4 == 0 &&
                    (batch <= 1 || sx % 4 == 0);
   if (transpose) {
@@ -615,15 +656,27 @@ cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batc
     // the tensor-core path: K (= rows) % 4 == 0 holds there.
     if (!vec || rows % 4 != 0) return cudaErrorInvalidValue;
     const dim3 grid{unsigned((cols + 63) / 64), unsigned((rows + 63) / 64), unsigned(batch)};
-    return launch_plain_pdl(split_tf32_transpose_kernel, grid, s, X, hi, lo, rows, cols, ld, sx);
+    return launch_plain_pdl(split_transpose_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
   }
   const long long n = vec ? rows * cols / 4 : rows * cols;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
-  if (vec) return launch_plain_pdl(split_tf32_vec_kernel, grid, s, X, hi, lo, rows, cols, ld, sx);
-  return launch_plain_pdl(split_tf32_kernel, grid, s, X, hi, lo, rows, cols, ld, sx);
+  if (vec) return launch_plain_pdl(split_vec_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
+  return launch_plain_pdl(split_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
+}
+}  // namespace
+
+cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
+                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
+  return launch_split_impl<float>(X, hi, lo, batch, rows, cols, ld, sx, transpose, s);
+}
+
+cudaError_t launch_split_bf16(const float* X, void* hi, void* lo, int64_t batch, int64_t rows, int64_t cols,
+                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
+  return launch_split_impl<__nv_bfloat16>(X, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), batch,
+                                          rows, cols, ld, sx, transpose, s);
 }
 
 }  // namespace cmpx

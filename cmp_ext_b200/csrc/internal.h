@@ -77,11 +77,17 @@ cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorM
 // tB/tB2 those of B, both packed K-major (B as [N][K]).
 cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
                              const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s);
+// bf16x3 variant: the same maps over packed bf16 hi/lo splits (box {64, 128}).
+cudaError_t launch_tc_bf16x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
+                             const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s);
 
 // Splits fp32 X [batch][rows][cols] (row stride ld, batch stride sx) into
 // packed tf32 hi and lo parts: [batch][rows][cols] contiguous, or with
 // transpose = true [batch][cols][rows] contiguous.
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
+                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s);
+// The same with bf16 hi = rn(x), lo = rn(x - hi) (hi, lo: __nv_bfloat16).
+cudaError_t launch_split_bf16(const float* X, void* hi, void* lo, int64_t batch, int64_t rows, int64_t cols,
                               int64_t ld, int64_t sx, bool transpose, cudaStream_t s);
 
 // Swap-AB stream-K kernel for skinny M (M <= 128), fp16/bf16.

@@ -54,7 +54,7 @@ cmpx_stream_t current_stream() {
 }
 
 // Test hook: force a kernel path for subsequent calls ("" / "auto", "tc",
-// "skinny", "simt").
+// "skinny", "simt", "bf16x3").
 int g_forced_path = CMPX_PATH_AUTO;
 
 void set_path(const std::string& p) {
@@ -62,7 +62,8 @@ void set_path(const std::string& p) {
   else if (p == "tc") g_forced_path = CMPX_PATH_TC;
   else if (p == "skinny") g_forced_path = CMPX_PATH_SKINNY;
   else if (p == "simt") g_forced_path = CMPX_PATH_SIMT;
-  else TORCH_CHECK(false, "unknown path '", p, "' (auto, tc, skinny, simt)");
+  else if (p == "bf16x3") g_forced_path = CMPX_PATH_BF16X3;
+  else TORCH_CHECK(false, "unknown path '", p, "' (auto, tc, skinny, simt, bf16x3)");
 }
 
 torch::Tensor linear(torch::Tensor input, torch::Tensor weight, c10::optional<torch::Tensor> bias) {
@@ -214,6 +215,7 @@ std::string matmul_path(int64_t M, int64_t N, int64_t K, const std::string& dtyp
     case CMPX_PATH_TC: return "tc";
     case CMPX_PATH_SKINNY: return "skinny";
     case CMPX_PATH_SIMT: return "simt";
+    case CMPX_PATH_BF16X3: return "bf16x3";
     default: return "invalid";
   }
 }

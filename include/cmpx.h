@@ -71,7 +71,11 @@ typedef enum {
   CMPX_PATH_AUTO = 0,
   CMPX_PATH_TC = 1,     /* tcgen05 persistent tile kernel (fp16/bf16) or 3xTF32 (fp32) */
   CMPX_PATH_SKINNY = 2, /* swap-AB stream-K tcgen05 kernel, M <= 128, fp16/bf16 */
-  CMPX_PATH_SIMT = 3    /* CUDA-core fallback */
+  CMPX_PATH_SIMT = 3,   /* CUDA-core fallback */
+  CMPX_PATH_BF16X3 = 4  /* fp32 only, opt-in: the tile kernel on bf16 hi/lo splits (hi*hi + hi*lo + lo*hi
+                           on the bf16 tensor rate, twice the tf32 rate); normwise error ~5e-6 against
+                           ~1e-6 for 3xTF32.  Needs K % 8 == 0.  AUTO never picks it; the environment
+                           variable CMPX_FORCE_PATH=bf16x3 makes fp32 calls take it. */
 } cmpx_path;
 
 /* General batched GEMM descriptor.  Strides are in elements. */

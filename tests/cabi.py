@@ -15,7 +15,7 @@ HEADER = os.path.join(REPO, "include", "cmpx.h")
 
 F16, BF16, F32 = 0, 1, 2
 B_KN, B_NK = 0, 1
-PATH_AUTO, PATH_TC, PATH_SKINNY, PATH_SIMT = 0, 1, 2, 3
+PATH_AUTO, PATH_TC, PATH_SKINNY, PATH_SIMT, PATH_BF16X3 = 0, 1, 2, 3, 4
 OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_NO_MEMORY, ERR_DEVICE, ERR_WORKSPACE, ERR_TOO_LARGE = range(8)
 
 

@@ -111,6 +111,12 @@ def test_path_selection():
     assert sel(path=cabi.PATH_SKINNY, M=129) == -1      # M > 128
     assert sel(path=cabi.PATH_TC, N=250, ldb=250, ldc=250) == -1
     assert sel(dtype=cabi.F32, path=cabi.PATH_SKINNY, lda=64, ldb=256, ldc=256) == -1
+    # bf16x3 (fp32 only, opt-in): packed bf16 rows need K % 8 == 0
+    f32 = dict(dtype=cabi.F32, M=512, N=512, K=512, lda=512, ldb=512, ldc=512)
+    assert sel(path=cabi.PATH_BF16X3, **f32) == cabi.PATH_BF16X3
+    assert sel(path=cabi.PATH_BF16X3, **{**f32, "K": 516, "lda": 516}) == -1
+    assert sel(path=cabi.PATH_BF16X3) == -1             # fp16 operands
+    assert sel(path=5) == -1
     assert sel(dtype=9) == -1
 
 

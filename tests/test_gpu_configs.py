@@ -97,14 +97,14 @@ def test_config4_decode_deterministic(cuda):
 
 
 def test_fp32_config5_paths_agree(cuda):
-    """Config 5 (1024-row slice) on the 3xTF32 tensor-core path and the
-    CUDA-core path: both inside the fp32 contract (the reference kernel's
+    """Config 5 (1024-row slice) on the 3xTF32 and bf16x3 tensor-core paths
+    and the CUDA-core path: all inside the fp32 contract (the reference kernel's
     own error at this K is about 3.7e-6, so the bound is ~1.37e-5)."""
     cfg = CONFIGS[5]
     A, B = make_inputs(cfg, "cuda", seed=3, m=1024)
     rows = _sample_rows(1024, 64)
     C64 = A[rows].double().cpu().numpy() @ B.double().cpu().numpy()
-    for path in (cabi.PATH_TC, cabi.PATH_SIMT):
+    for path in (cabi.PATH_TC, cabi.PATH_BF16X3, cabi.PATH_SIMT):
         C = _run(A, B, path=path)
         err = o.normwise_err(C[rows].double().cpu().numpy(), C64)
         print(f"config5 path {path}: err {err:.3e}")

@@ -130,6 +130,39 @@ def test_tf32x3_path(cuda, b_layout, shape):
     assert err < 5e-6
 
 
+@pytest.mark.parametrize("b_layout", [cabi.B_KN, cabi.B_NK])
+@pytest.mark.parametrize("shape", [(256, 256, 256), (300, 260, 136), (128, 128, 4096), (257, 384, 512),
+                                   (1000, 136, 72)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_bf16x3_path(cuda, b_layout, shape):
+    """fp32 through bf16 hi/lo splits: truncation leaves ~2^-17 per
+    product, so the normwise error sits near 5e-6, inside the fp32 contract
+    (reference kernel error + 1e-5, checked by check_case)."""
+    M, N, K = shape
+    err = check_case(M, N, K, torch.float32, b_layout=b_layout, path=cabi.PATH_BF16X3)
+    assert err < 1e-5
+
+
+def test_bf16x3_workspace_and_odd_k(cuda):
+    g = torch.Generator().manual_seed(11)
+    A = _rand((256, 520), torch.float32, g).cuda()
+    B = _rand((520, 384), torch.float32, g).cuda()
+    C = torch.empty((256, 384), device="cuda")
+    args = cabi.gemm_args(A, B, C, path=cabi.PATH_BF16X3)
+    need = cabi.lib().cmpx_gemm_workspace_size(ctypes.byref(args))
+    assert need == 2 * (256 * 520 * 2) + 2 * (520 * 384 * 2)  # bf16 hi + lo of A and B (256-byte rounded)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    args = cabi.gemm_args(A, B, C, path=cabi.PATH_BF16X3, workspace=ws.data_ptr(), workspace_bytes=need)
+    assert cabi.gemm(args) == cabi.OK
+    torch.cuda.synchronize()
+    want = A.double() @ B.double()
+    assert o.normwise_err(C.double().cpu().numpy(), want.cpu().numpy()) < 1e-5
+    # K % 8 != 0: packed bf16 rows would not be 16-byte multiples
+    A2 = _rand((128, 132), torch.float32, g).cuda()
+    B2 = _rand((132, 128), torch.float32, g).cuda()
+    run_cabi(A2, B2, path=cabi.PATH_BF16X3, expect=cabi.ERR_UNSUPPORTED)
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("shape", [(257, 383, 511), (5, 7, 3), (70, 130, 33), (1, 1, 1)],
                          ids=lambda s: "x".join(map(str, s)))

@@ -21,6 +21,8 @@
 //   B tile, [K,N] source: BN/CW chunks of [BK rows][128 B of N], MN-major,
 //           LBO = chunk bytes, SBO = 1024   (CW = 128 B / elem)
 //   B tile, [N,K] source: [BN rows][128 B of K], K-major, SBO = 1024
+#include <cstdlib>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -43,7 +45,8 @@ struct TcParams {
 };
 
 // FMT: 0 = f16, 1 = bf16, 2 = tf32x3 (fp32 in/out, tf32 hi/lo operands),
-//      3 = bf16x3 (fp32 in/out, bf16 hi/lo operands)
+//      3 = bf16x3 (fp32 in/out, bf16 hi/lo operands), 4 = bf16x3 with the
+//      two hi-A products in one MMA of width 2*BN (see below)
 template <int FMT, bool B_KMAJOR, int BN_, int STAGES_>
 struct TcCfg {
   static constexpr bool SPLIT = FMT >= 2;     // fp32 product from hi/lo operand splits
@@ -66,12 +69,19 @@ struct TcCfg {
   // K), each summed afresh in TMEM and added into fp32 registers by the
   // epilogue with IEEE round-to-nearest; four buffers let the MMA run three
   // chunks ahead.
-  static constexpr int NACC = SPLIT ? 4 : 2;
+  // FMT 4 issues Ah*[Bh | Bl] as one MMA of width 2*BN (B's hi and lo
+  // blocks are adjacent K-major rows in shared memory), then Al*Bh into the
+  // first half: two accumulator halves per tile that the epilogue adds.
+  static constexpr bool NCAT = FMT == 4;
+  static constexpr int ACC_COLS = NCAT ? 2 * BN : BN;
+  static constexpr int NACC = NCAT ? 2 : SPLIT ? 4 : 2;
   static constexpr int KCH = SPLIT ? 128 / BK : (1 << 30);
-  static constexpr uint32_t TMEM_COLS = NACC * BN;
+  static constexpr uint32_t TMEM_COLS = NACC * ACC_COLS;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 512;
   // operand formats: 0 = f16, 1 = bf16 (kind::f16), 2 = tf32 (kind::tf32)
-  static constexpr uint32_t IDESC = make_idesc(FMT == 2 ? 2u : FMT == 0 ? 0u : 1u, 0u, B_KMAJOR ? 0u : 1u, BM, BN);
+  static constexpr uint32_t IDESC =
+      make_idesc(FMT == 2 ? 2u : FMT == 0 ? 0u : 1u, 0u, B_KMAJOR ? 0u : 1u, BM, NCAT ? 2 * BN : BN);
+  static constexpr uint32_t IDESC_HALF = make_idesc(1u, 0u, 0u, BM, BN);  // FMT 4: Al*Bh
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert(B_KMAJOR || BN % CW == 0, "BN must be whole N-major chunks");
   // An MN-major tf32 operand needs the 128B swizzle with 32B atoms; the
@@ -304,7 +314,7 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+          const uint32_t d_tmem = tmem_base + uint32_t(acc * Cfg::ACC_COLS);
           const int kend = min(num_kb, kc + Cfg::KCH);
           for (int kb = kc; kb < kend; ++kb) {
             if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
@@ -330,6 +340,10 @@ __global__ void __launch_bounds__(192, 1)
                   mma_tf32(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
                   mma_tf32(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
                   mma_tf32(d_tmem, adesc, bdesc, Cfg::IDESC, 1u);
+                } else if constexpr (Cfg::NCAT) {
+                  (void)bdesc_lo;
+                  mma_f16(d_tmem, adesc, bdesc, Cfg::IDESC, accum);         // [Ah*Bh | Ah*Bl]
+                  mma_f16(d_tmem, adesc_lo, bdesc, Cfg::IDESC_HALF, 1u);    // + Al*Bh
                 } else {
                   mma_f16(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
                   mma_f16(d_tmem, adesc, bdesc_lo, Cfg::IDESC, 1u);
@@ -384,14 +398,15 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+          const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * Cfg::ACC_COLS);
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = 0; c < Cfg::ACC_COLS / 32; ++c) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(t_row + c * 32, r);
             tmem_ld_wait();
+            const int o = (c * 32) % BN;  // FMT 4: the second half adds onto the same columns
 #pragma unroll
-            for (int i = 0; i < 32; ++i) racc[c * 32 + i] = __fadd_rn(racc[c * 32 + i], __uint_as_float(r[i]));
+            for (int i = 0; i < 32; ++i) racc[o + i] = __fadd_rn(racc[o + i], __uint_as_float(r[i]));
           }
           tc_fence_before();
           mbar_arrive(&acc_empty[acc]);
@@ -497,6 +512,12 @@ cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtenso
 
 cudaError_t launch_tc_bf16x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
                              const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  static int ncat = -1;
+  if (ncat < 0) {
+    const char* e = std::getenv("CMPX_BF16X3_NCAT");
+    ncat = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  if (ncat) return launch_tc_impl<4, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
   return launch_tc_impl<3, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
 }
 

@@ -32,3 +32,13 @@ def test_skinny_unit_width_variant(cuda, ns):
                         os.path.join(HERE, "test_gpu_parity.py"), "-k", "skinny"],
                        env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+def test_bf16x3_three_mma_variant(cuda):
+    """The fp32 bf16x3 kernel in its three-MMA form (lo*hi, hi*lo, hi*hi at
+    width 128); the default form issues hi*[hi | lo] at width 256 plus lo*hi."""
+    env = dict(os.environ, CMPX_BF16X3_NCAT="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.join(HERE, "test_gpu_parity.py"), "-k", "bf16x3"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

@@ -428,9 +428,14 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   const float* fA = reinterpret_cast<const float*>(g.A);
   const float* fB = reinterpret_cast<const float*>(g.B);
   cudaError_t e;
+  // bf16x3 keeps the splits of a [K,N] B N-major (no transpose) when packed
+  // rows of N are 16-byte multiples and the source suits the vector split.
+  const bool b_nmajor = bf && !g.b_kmajor && g.N % 8 == 0 && g.ldb % 4 == 0 && aligned16(g.B) &&
+                        (g.batch <= 1 || g.sb % 4 == 0);
   if (bf) {
     e = launch_split_bf16(fA, a_hi, a_lo, a_batch, g.M, g.K, g.lda, g.sa, false, s);
-    if (e == cudaSuccess) e = launch_split_bf16(fB, b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb, !g.b_kmajor, s);
+    if (e == cudaSuccess)
+      e = launch_split_bf16(fB, b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb, !g.b_kmajor && !b_nmajor, s);
   } else {
     e = launch_split_tf32(fA, static_cast<float*>(a_hi), static_cast<float*>(a_lo), a_batch, g.M, g.K, g.lda, g.sa,
                           false, s);
@@ -445,9 +450,14 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   const uint32_t box_k = bf ? 64 : 32;          // one 128-byte swizzle row of K
   if ((st = encode_3d(&tA, op, a_hi, g.K, g.M, a_batch, g.K, sa, box_k, 128)) != CMPX_OK) return st;
   if ((st = encode_3d(&tA2, op, a_lo, g.K, g.M, a_batch, g.K, sa, box_k, 128)) != CMPX_OK) return st;
-  if ((st = encode_3d(&tB, op, b_hi, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
-  if ((st = encode_3d(&tB2, op, b_lo, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
-  if (bf) return cuda_status(launch_tc_bf16x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));
+  if (b_nmajor) {  // [K][N] splits: 64-column x 64-row boxes, N-major chunks
+    if ((st = encode_3d(&tB, op, b_hi, g.N, g.K, g.batch, g.N, sb, 64, 64)) != CMPX_OK) return st;
+    if ((st = encode_3d(&tB2, op, b_lo, g.N, g.K, g.batch, g.N, sb, 64, 64)) != CMPX_OK) return st;
+  } else {
+    if ((st = encode_3d(&tB, op, b_hi, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
+    if ((st = encode_3d(&tB2, op, b_lo, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
+  }
+  if (bf) return cuda_status(launch_tc_bf16x3(g, tA, tA2, tB, tB2, b_nmajor, d->info, d->err_word, s));
   return cuda_status(launch_tc_tf32x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));
 }
 

@@ -81,12 +81,15 @@ struct TcCfg {
   // operand formats: 0 = f16, 1 = bf16 (kind::f16), 2 = tf32 (kind::tf32)
   static constexpr uint32_t IDESC =
       make_idesc(FMT == 2 ? 2u : FMT == 0 ? 0u : 1u, 0u, B_KMAJOR ? 0u : 1u, BM, NCAT ? 2 * BN : BN);
-  static constexpr uint32_t IDESC_HALF = make_idesc(1u, 0u, 0u, BM, BN);  // FMT 4: Al*Bh
+  static constexpr uint32_t IDESC_HALF = make_idesc(1u, 0u, B_KMAJOR ? 0u : 1u, BM, BN);  // FMT 4: Al*Bh
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert(B_KMAJOR || BN % CW == 0, "BN must be whole N-major chunks");
   // An MN-major tf32 operand needs the 128B swizzle with 32B atoms; the
   // split pre-pass stores fp32 B K-major instead, so that form is not built.
-  static_assert(!SPLIT || B_KMAJOR, "the split formats take B K-major");
+  // bf16 splits of a [K,N] B stay N-major (the 16-bit MN-major layout above;
+  // for FMT 4 the lo chunks follow the hi chunks at the same LBO, so hi|lo
+  // is one operand of width 2*BN).
+  static_assert(FMT != 2 || B_KMAJOR, "3xTF32 takes B K-major");
 };
 
 __device__ __forceinline__ void decode_tile(int t, const TcParams& p, int& b, int& tm, int& tn) {
@@ -334,7 +337,9 @@ __global__ void __launch_bounds__(192, 1)
               const uint32_t accum = (kb != kc || ks != 0) ? 1u : 0u;
               if constexpr (Cfg::SPLIT) {
                 const uint64_t adesc_lo = make_sdesc_sw128(a_addr + Cfg::A_BYTES + ks * 32, 16, 1024);
-                const uint64_t bdesc_lo = make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * 32, 16, 1024);
+                const uint64_t bdesc_lo =
+                    B_KMAJOR ? make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * 32, 16, 1024)
+                             : make_sdesc_sw128(b_addr + Cfg::B_BYTES + ks * Cfg::KSTEP_BYTES_MN, Cfg::CHUNK_BYTES, 1024);
                 // small cross terms first, then the dominant hi*hi product
                 if constexpr (FMT == 2) {
                   mma_tf32(d_tmem, adesc_lo, bdesc, Cfg::IDESC, accum);
@@ -511,7 +516,8 @@ cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtenso
 }
 
 cudaError_t launch_tc_bf16x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
-                             const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+                             const CUtensorMap& tB2, bool b_nmajor, const DeviceInfo& dev, int* dev_err,
+                             cudaStream_t s) {
   static int ncat = -1;
   if (ncat < 0) {
     // Measured on a B200 (8192^3, isolated launches): 2.90 ms with the
@@ -519,6 +525,10 @@ cudaError_t launch_tc_bf16x3(const Gemm& g, const CUtensorMap& tA, const CUtenso
     // power-capped clock; CMPX_BF16X3_NCAT=0 selects the three-MMA form.
     const char* e = std::getenv("CMPX_BF16X3_NCAT");
     ncat = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  if (b_nmajor) {
+    if (ncat) return launch_tc_impl<4, false, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
+    return launch_tc_impl<3, false, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
   }
   if (ncat) return launch_tc_impl<4, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
   return launch_tc_impl<3, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
@@ -567,30 +577,35 @@ struct Vec4<__nv_bfloat16> {
 };
 
 // X [rows][cols] (row stride ld) -> packed hi, lo [rows][cols].  Vector
-// form: cols % 4 == 0, ld % 4 == 0 and X 16-byte aligned.
+// form: cols % 4 == 0, ld % 4 == 0 and X 16-byte aligned.  Blocks stride over
+// rows and threads over a row's float4s, so no index needs a division.
 template <typename S>
 __global__ void split_vec_kernel(const float* __restrict__ X, S* __restrict__ hi, S* __restrict__ lo,
                                  long long rows, long long cols, long long ld, long long sx) {
   pdl_trigger();
   pdl_wait();  // X may be the previous kernel's output
   const long long b = blockIdx.y;
-  const long long c4 = cols / 4, n4 = rows * c4;
+  const long long c4 = cols / 4;
   const float* xb = X + b * sx;
   S* hb = hi + b * rows * cols;
   S* lb = lo + b * rows * cols;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / c4, c = i - r * c4;
-    const float4 x = __ldcs(reinterpret_cast<const float4*>(xb + r * ld) + c);
-    Vec4<S> h, l;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float4* xr = reinterpret_cast<const float4*>(xb + r * ld);
+    S* hr = hb + r * cols;
+    S* lr = lb + r * cols;
+    for (long long c = threadIdx.x; c < c4; c += blockDim.x) {
+      const float4 x = __ldcs(xr + c);
+      Vec4<S> h, l;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      S hj, lj;
-      split1((&x.x)[j], hj, lj);
-      h.set(j, hj);
-      l.set(j, lj);
+      for (int j = 0; j < 4; ++j) {
+        S hj, lj;
+        split1((&x.x)[j], hj, lj);
+        h.set(j, hj);
+        l.set(j, lj);
+      }
+      h.store(hr + 4 * c);
+      l.store(lr + 4 * c);
     }
-    h.store(hb + 4 * i);
-    l.store(lb + 4 * i);
   }
 }
 
@@ -682,12 +697,17 @@ cudaError_t launch_split_impl(const float* X, S* hi, S* lo, int64_t batch, int64
     const dim3 grid{unsigned((cols + 63) / 64), unsigned((rows + 63) / 64), unsigned(batch)};
     return launch_plain_pdl(split_transpose_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
   }
-  const long long n = vec ? rows * cols / 4 : rows * cols;
+  if (vec) {
+    // one block per row (up to 16 per SM resident), grid-strided beyond that
+    const long long blocks = rows < 148 * 16 ? (rows > 0 ? rows : 1) : 148 * 16;
+    const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
+    return launch_plain_pdl(split_vec_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
+  }
+  const long long n = rows * cols;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
-  if (vec) return launch_plain_pdl(split_vec_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
   return launch_plain_pdl(split_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
 }
 }  // namespace

@@ -77,9 +77,11 @@ cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorM
 // tB/tB2 those of B, both packed K-major (B as [N][K]).
 cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
                              const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s);
-// bf16x3 variant: the same maps over packed bf16 hi/lo splits (box {64, 128}).
+// bf16x3 variant: the same maps over packed bf16 hi/lo splits (box {64, 128}),
+// or with b_nmajor the splits of B kept [K][N] (box {64 of N, 64 of K}).
 cudaError_t launch_tc_bf16x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
-                             const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s);
+                             const CUtensorMap& tB2, bool b_nmajor, const DeviceInfo& dev, int* dev_err,
+                             cudaStream_t s);
 
 // Splits fp32 X [batch][rows][cols] (row stride ld, batch stride sx) into
 // packed tf32 hi and lo parts: [batch][rows][cols] contiguous, or with

@@ -143,6 +143,20 @@ def test_bf16x3_path(cuda, b_layout, shape):
     assert err < 1e-5
 
 
+@pytest.mark.parametrize("n", [136, 260])  # N-major splits of B / transposed splits (N % 8 != 0)
+def test_bf16x3_batched(cuda, n):
+    g = torch.Generator().manual_seed(12)
+    Bt, M, K = 3, 200, 328
+    A = _rand((Bt, M, K), torch.float32, g).cuda()
+    B = _rand((Bt, K, n), torch.float32, g).cuda()
+    C = torch.empty((Bt, M, n), device="cuda")
+    args = cabi.gemm_args(A[0], B[0], C[0], batch=Bt, sa=M * K, sb=K * n, sc=M * n, path=cabi.PATH_BF16X3)
+    assert cabi.gemm(args) == cabi.OK
+    torch.cuda.synchronize()
+    want = torch.bmm(A.double(), B.double())
+    assert o.normwise_err(C.double().cpu().numpy(), want.cpu().numpy()) < 1e-5
+
+
 def test_bf16x3_workspace_and_odd_k(cuda):
     g = torch.Generator().manual_seed(11)
     A = _rand((256, 520), torch.float32, g).cuda()

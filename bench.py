@@ -71,52 +71,116 @@ def traffic_per_launch(key: str):
 
 
 # ------------------------------------------------------------------ clocks
-class ClockSampler:
-    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
-        self.proc = None
+
+class ClockSampler:
+    """SM clock, power and throttle reasons of one GPU, sampled every ~5 ms
+    by a thread (NVML) between start() and stop(): only the timed region is
+    sampled, so even a 30 ms region yields a handful of samples.  Falls back
+    to `nvidia-smi -lms 100` when NVML is unavailable."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.samples = []
+        self._stop = None
+        self._thread = None
+        self._smi = None
+        self.handle = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+            self.nvml = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.handle = None
+
+    def _poll(self):
+        import threading  # noqa: F401
+
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                pw = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, pw, rs))
+            except Exception:
+                pass
+            self._stop.wait(0.005)
 
     def start(self):
-        try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.idx), "-lms", "100"], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+        self.samples = []
+        if self.handle is not None:
+            import threading
+
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
+        else:
+            try:
+                self._path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+                self._f = open(self._path, "w")
+                self._smi = subprocess.Popen(
+                    ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active",
+                     "--format=csv,noheader,nounits", "-i", str(self.device.index or 0), "-lms", "100"],
+                    stdout=self._f, stderr=subprocess.DEVNULL)
+            except OSError:
+                self._smi = None
 
     def stop(self):
-        if self.proc is None:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
+            self._thread = None
+            rows = self.samples
+            max_mhz = self.max_mhz
+            src = "nvml, ~5 ms"
+        elif self._smi is not None:
+            self._smi.terminate()
+            try:
+                self._smi.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._smi.kill()
+            self._f.close()
+            rows, max_mhz = [], 0.0
+            with open(self._path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    try:
+                        rows.append((float(parts[0]), float(parts[2]), int(parts[3], 16)))
+                        max_mhz = max(max_mhz, float(parts[1]))
+                    except (ValueError, IndexError):
+                        continue
+            os.unlink(self._path)
+            self._smi = None
+            src = "nvidia-smi, 100 ms"
+        else:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.f.close()
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 10:
-                    continue
-                try:
-                    rows.append((float(parts[2]), float(parts[3]), float(parts[4]) if parts[4] not in ("[N/A]", "N/A") else 0.0, parts[6:10]))
-                except ValueError:
-                    continue
-        os.unlink(self.path)
         if not rows:
             return None
-        loaded = [r for r in rows if r[2] > 200.0] or rows
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(loaded)}
+        reasons = sorted({n for r in rows for n, bit in REASON_BITS.items() if r[2] & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max_mhz,
+                "sm_mhz_min": min(r[0] for r in rows), "power_w_max": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows), "sampler": src, "window": "timed region only"}
+
+
+def pick_peak(P, clocks, div=1.0):
+    """Burst or sustained GEMM peak, chosen from the state the run was
+    measured in: sustained when the power cap was active or the SM clock sat
+    well below its maximum, burst otherwise."""
+    burst = P["bf16_tflops"] / div
+    sustained = P.get("bf16_tflops_sustained", P["bf16_tflops"]) / div
+    if clocks is None:
+        return sustained, "sustained (no clock record)"
+    capped = "sw_power_cap" in clocks["reasons"] or clocks["sm_mhz"] < 0.85 * max(clocks["sm_max_mhz"], 1.0)
+    return (sustained, "sustained (power-capped clocks seen)") if capped else (burst, "burst (clocks at max)")
 
 
 # ------------------------------------------------------------------ helpers
@@ -271,6 +335,213 @@ def run_reference(args):
     return 0
 
 
+class Timer:
+    """Times K back-to-back steps on this rank's stream, max over ranks,
+    after holding the GPU busy for `hold_s` seconds (so every run, whatever
+    N, is measured in the same power state), with the clocks sampled inside
+    the timed region only."""
+
+    def __init__(self, world, device, quick, hold_s):
+        self.world, self.device, self.quick, self.hold_s = world, device, quick, hold_s
+        self.stream = torch.cuda.current_stream(device)
+        self.clock = None if quick else ClockSampler(device)
+
+    def hold(self, step, warmup):
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        if self.quick:
+            return
+        t0 = time.perf_counter()
+        n = 1
+        while time.perf_counter() - t0 < self.hold_s:
+            for _ in range(n):
+                step()
+            torch.cuda.synchronize()
+            n = min(n * 2, 64)
+
+    def run(self, step, steps, warmup, flush=None):
+        """(ms of the K steps minus their L2 flushes, clocks)."""
+        self.hold(step, warmup)
+        flush_ms = 0.0
+        if flush is not None:
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(self.stream)
+            for _ in range(steps):
+                flush.fill_(1)
+            f1.record(self.stream)
+            torch.cuda.synchronize()
+            flush_ms = f0.elapsed_time(f1)
+            for _ in range(3):
+                step()
+        barrier(self.world)
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if self.clock is not None:
+            self.clock.start()
+        ev0.record(self.stream)
+        for _ in range(steps):
+            if flush is not None:
+                flush.fill_(1)
+            step()
+        ev1.record(self.stream)
+        torch.cuda.synchronize()
+        clocks = self.clock.stop() if self.clock is not None else None
+        barrier(self.world)
+        ms = max(ev0.elapsed_time(ev1) - flush_ms, 1e-6)
+        return max_over_ranks(ms, self.world, self.device), clocks
+
+    def isolated(self, fn, reps, flush=None):
+        """Median event time of single launches with the GPU idle around each."""
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        out = []
+        for _ in range(reps):
+            if flush is not None:
+                flush.fill_(1)
+            torch.cuda.synchronize()
+            time.sleep(0.002)
+            k0.record(self.stream)
+            fn()
+            k1.record(self.stream)
+            torch.cuda.synchronize()
+            out.append(k0.elapsed_time(k1))
+        return statistics.median(out)
+
+
+def rows_err(C, A, B, rows=64):
+    """Normwise error max|C - C64| / max|C64| of a spread sample of C's rows
+    against the fp64 product of the same rows (computed on the GPU)."""
+    M = A.shape[0]
+    idx = torch.linspace(0, M - 1, min(rows, M), device=A.device).long()
+    ref = A[idx].double() @ B.double()
+    return float((C[idx].double() - ref).abs().max() / ref.abs().max())
+
+
+def tensor_record(cfg, m, ms_step, clocks, P, kernel, launch_ms=None, extra=None):
+    """One measured workload: TFLOP/s (or GB/s) and its roofline fraction."""
+    e = torch.empty((), dtype=cfg.dtype).element_size()
+    rec = {"workload": f"config{cfg.cid}: {cfg.name}" + ("" if m == cfg.M else f" ({m} rows)"), "kernel": kernel,
+           "ms_per_step": ms_step, "clocks": clocks}
+    if cfg.bound == "hbm":
+        byt = (m * cfg.K + cfg.K * cfg.N + m * cfg.N) * e
+        ach = byt / (ms_step / 1e3) / 1e9
+        rec.update({"value": ach, "unit": "GB/s", "roofline": {"bound": "hbm", "achieved": ach, "peak": P["hbm_gbs"],
+                    "peak_kind": "measured copy", "frac": ach / P["hbm_gbs"], "unit": "GB/s"}})
+        if launch_ms:
+            rec["isolated_launch"] = {"ms": launch_ms, "achieved": byt / (launch_ms / 1e3) / 1e9,
+                                      "frac": byt / (launch_ms / 1e3) / 1e9 / P["hbm_gbs"]}
+    else:
+        fl = 2.0 * m * cfg.N * cfg.K
+        ach = fl / (ms_step / 1e3) / 1e12
+        div = 2.0 if cfg.dtype == torch.float32 else 1.0  # tf32 tensor rate = bf16 / 2
+        peak, kind = pick_peak(P, clocks, div)
+        rec.update({"value": ach, "unit": "TFLOP/s",
+                    "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "peak_kind": kind,
+                                 "frac": ach / peak, "unit": "TFLOP/s",
+                                 "tflops_per_mhz": (ach / clocks["sm_mhz"]) if clocks else None}})
+        if cfg.dtype == torch.float32:
+            rec["roofline"]["note"] = ("peak = bf16 figure / 2 (tf32 rate); the tensor pipe does 3 MMAs per "
+                                       "product, so frac <= 1/3 at best for 3xTF32")
+        if launch_ms:
+            rec["isolated_launch"] = {"ms": launch_ms, "achieved": fl / (launch_ms / 1e3) / 1e12,
+                                      "peak": P["bf16_tflops"] / div,
+                                      "frac": fl / (launch_ms / 1e3) / 1e12 / (P["bf16_tflops"] / div)}
+    if extra:
+        rec.update(extra)
+    return rec
+
+
+def sub_workload(cid, timer, P, args, device, world, rank, path=None, steps=None, sharded=False):
+    """Measures one more config in the same run (resident inputs, same timing
+    rules) and returns its record."""
+    from cmp_ext_b200 import _cmpext3 as ext
+
+    cfg = CONFIGS[cid]
+    r0, r1 = shard_rows(cfg.M, world, rank) if sharded else (0, cfg.M)
+    m = r1 - r0
+    A, B = make_inputs(cfg, device, seed=0, m=m, a_seed=1000 + rank)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device) if cfg.bytes(m) <= 189e6 else None
+    op = op_for(cfg.dtype)
+    prev = None
+    if path is not None:
+        ext._set_path(path)
+    try:
+        out = {}
+
+        def step():
+            out["C"] = op(A, B)
+
+        K = steps or max(3, min(args.steps, 20))
+        ms, clocks = timer.run(step, K, 3, flush)
+        launch_ms = timer.isolated(step, 5 if K >= 5 else 2, flush)
+        err = rows_err(out["C"], A, B)
+        kern = kernel_name(cfg, m) if path is None else {"simt": "gemm_simt_kernel", "tc": kernel_name(cfg, m),
+                                                         "bf16x3": "gemm_tc_kernel(bf16x3)"}[path]
+        rec = tensor_record(cfg, m, ms / K, clocks, P, kern, launch_ms,
+                            {"err_vs_fp64_rows": err, "steps": K, "l2": "flushed" if flush is not None else
+                             "inputs larger than L2"})
+        if sharded:
+            job = 2.0 * cfg.M * cfg.N * cfg.K
+            rec["job_value"] = job / (ms / K / 1e3) / 1e12
+            rec["parallelism"] = f"M-shard x{world}, no gather"
+        if path == "simt":
+            # CUDA-core fp32: 2 FLOP per FMA, 128 FMA lanes per SM per clock
+            sm = clocks["sm_mhz"] if clocks else 1965.0
+            pk = 2.0 * 128 * torch.cuda.get_device_properties(device).multi_processor_count * sm * 1e6 / 1e12
+            rec["roofline"] = {"bound": "fp32 CUDA cores", "achieved": rec["value"], "peak": pk,
+                               "peak_kind": f"nominal FFMA rate at the observed {sm:.0f} MHz",
+                               "frac": rec["value"] / pk, "unit": "TFLOP/s"}
+        return rec
+    finally:
+        if path is not None:
+            ext._set_path(prev or "auto")
+        del A, B
+        torch.cuda.empty_cache()
+
+
+def gathered_record(cfg, transport, timer, P, args, device, world, rank):
+    """Config 3 M-sharded with the all-gather of C (every rank ends with the
+    whole C), and a check of the gathered C: sampled rows of every rank's
+    block against the fp64 product of that rank's A rows, which this rank
+    regenerates from the rank's seed."""
+    from cmp_ext_b200.distributed import gather_output, sharded_matmul
+
+    S = cfg.M // world
+    A, B = make_inputs(cfg, device, seed=0, m=S, a_seed=1000 + rank)
+    if transport == "nvlink":
+        Cfull = gather_output(cfg.M, cfg.N, cfg.dtype, device)
+    else:
+        Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
+
+    def step():
+        sharded_matmul(A, B, M=cfg.M, gather=True, out=Cfull, transport=transport)
+
+    K = max(3, min(args.steps, 20))
+    ms, clocks = timer.run(step, K, 3)
+    torch.cuda.synchronize()
+    errs = []
+    for q in range(world):
+        Aq, _ = make_inputs(cfg, device, seed=0, m=S, a_seed=1000 + q)
+        idx = torch.linspace(0, S - 1, 8, device=device).long()
+        ref = Aq[idx].double() @ B.double()
+        got = Cfull[q * S + idx].double()
+        errs.append(float((got - ref).abs().max() / ref.abs().max()))
+        del Aq
+    ok = max(errs) <= 1e-2  # the build's bf16 error is ~3e-3; a missing or stale block gives ~1
+    okt = torch.tensor([1.0 if ok else 0.0], device=device)
+    if world > 1:
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    rec = tensor_record(cfg, S, ms / K, clocks, P, kernel_name(cfg, S) + f" + {transport} all-gather")
+    job = 2.0 * cfg.M * cfg.N * cfg.K / (ms / K / 1e3) / 1e12
+    rec.update({"job_value": job, "unit": "TFLOP/s", "transport": transport,
+                "check": {"all_ranks_ok": bool(okt.item() == 1.0), "max_err_vs_fp64_rows": max(errs),
+                          "what": "8 rows of every rank's block of the gathered C on this rank vs fp64"},
+                "bytes_in_per_rank": (world - 1) * S * cfg.N * torch.empty((), dtype=cfg.dtype).element_size()})
+    del A, B, Cfull
+    torch.cuda.empty_cache()
+    return rec
+
+
 def run_ours(args):
     world, rank, local = dist_setup(args)
     device = torch.device("cuda", local)
@@ -281,14 +552,18 @@ def run_ours(args):
     m = r1 - r0 if args.rows is None else args.rows
     if args.quick:
         args.no_e2e = args.no_cpu = True
+        args.sub = "none"
     op = op_for(cfg.dtype)
     if cfg.dtype == torch.float32 and args.f32_path == "bf16x3":
         from cmp_ext_b200 import _cmpext3 as ext
 
         ext._set_path("bf16x3")  # every fp32 call of this process, e2e included
+    P, peak_src = peaks()
+    timer = Timer(world, device, args.quick, args.hold)
 
-    # Inputs resident in HBM (drawn on the device, seeded per config).
-    A, B = make_inputs(cfg, device, seed=0, m=m)
+    # Inputs resident in HBM (drawn on the device; the same B on every rank,
+    # a different A shard per rank).
+    A, B = make_inputs(cfg, device, seed=0, m=m, a_seed=1000 + rank)
     A = A.contiguous()
     flush = None
     if cfg.bytes(m) <= 126e6 * 1.5:
@@ -302,67 +577,18 @@ def run_ours(args):
         else:
             Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
 
+    last = {}
+
     def step():
-        if flush is not None:
-            flush.fill_(1)
         if gather:
             sharded_matmul(A, B, M=cfg.M, gather=True, chunks=args.chunks, out=Cfull, transport=args.transport)
         else:
-            op(A, B)
+            last["C"] = op(A, B)
 
-    stream = torch.cuda.current_stream()
-    clock = ClockSampler(local)
-    if not args.quick:
-        clock.start()
-    t_start = time.perf_counter()
-    for _ in range(args.warmup if args.quick else max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    # keep warming until the clock sampler has produced samples (~0.5 s)
-    while not args.quick and time.perf_counter() - t_start < 0.6:
-        step()
-        torch.cuda.synchronize()
-
-    # kernel-only timing: events bracket exactly the K launches on this stream
-    barrier(world)
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    flush_ms = 0.0
-    if flush is not None:
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for _ in range(args.steps):
-            flush.fill_(1)
-        f1.record(stream)
-        torch.cuda.synchronize()
-        flush_ms = f0.elapsed_time(f1)
-    barrier(world)
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    ms_total = ev0.elapsed_time(ev1)
-    barrier(world)
-    clocks = clock.stop()
-    ms_gemm_total = max(ms_total - flush_ms, 1e-6)
-    ms_total = max_over_ranks(ms_total, world, device)
-    ms_gemm = max_over_ranks(ms_gemm_total, world, device)
-
-    # Dominant kernel alone (average launch duration, events on its stream).
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kreps = 1 if args.quick else max(5, min(args.steps, 50))
-    launch_ms = []
-    for _ in range(kreps):
-        if flush is not None:
-            flush.fill_(1)
-        k0.record(stream)
-        op(A, B)
-        k1.record(stream)
-        torch.cuda.synchronize()
-        launch_ms.append(k0.elapsed_time(k1))
-    launch_ms = statistics.median(launch_ms)
+    ms_gemm, clocks = timer.run(step, args.steps, args.warmup if args.quick else max(3, args.warmup), flush)
+    ms_total = ms_gemm
+    launch_ms = timer.isolated(lambda: op(A, B), 1 if args.quick else max(5, min(args.steps, 20)), flush)
+    err = None if gather or args.quick else rows_err(last["C"], A, B)
 
     M_job = cfg.M if args.rows is None else args.rows * world
     step_flops = 2.0 * M_job * cfg.N * cfg.K  # whole job (all ranks)
@@ -374,52 +600,81 @@ def run_ours(args):
         value = step_flops * args.steps / (ms_gemm / 1e3) / 1e12
     ms_per_step = ms_gemm / args.steps
 
-    P, peak_src = peaks()
     # Average launch duration of the dominant kernel over the timed region:
-    # when a step is that one launch and nothing runs between steps, it is
-    # the timed region divided by K; otherwise the isolated launch above.
-    one_launch = launches_per_step(cfg, args.rows) == 1 and flush is None and not gather
-    avg_launch_ms = ms_gemm / args.steps if one_launch else launch_ms
-    timing = ("timed region / K (back-to-back launches)" if one_launch
+    # when a step is that one launch, it is the timed region divided by K;
+    # otherwise the isolated launch.
+    one_launch = launches_per_step(cfg, args.rows) == 1 and not gather
+    avg_launch_ms = ms_per_step if one_launch else launch_ms
+    timing = ("timed region / K (back-to-back launches, L2 flush time subtracted)" if one_launch
               else "median of isolated launches (events around each)")
     scale = 1e9 if cfg.bound == "hbm" else 1e12
     if cfg.bound == "hbm":
         per_launch = cfg.bytes(m)
         peak = peak_isolated = P["hbm_gbs"]
-        peak_kind = "copy"
+        peak_kind = "measured copy"
         runit, rbound = "GB/s", "hbm"
     else:
-        # a kernel timed back to back for the whole timed region runs under
-        # the power cap: the sustained GEMM figure; an isolated launch: burst
         per_launch = 2.0 * m * cfg.N * cfg.K
         div = 2.0 if cfg.dtype == torch.float32 else 1.0  # tf32 rate = bf16 / 2
-        burst = P["bf16_tflops"] / div
-        sustained = P.get("bf16_tflops_sustained", P["bf16_tflops"]) / div
-        peak, peak_kind = (sustained, "sustained") if one_launch else (burst, "burst")
-        peak_isolated = burst
+        peak, peak_kind = pick_peak(P, clocks if one_launch else None, div)
+        if not one_launch:
+            peak, peak_kind = P["bf16_tflops"] / div, "burst (isolated launch)"
+        peak_isolated = P["bf16_tflops"] / div
         runit, rbound = "TFLOP/s", "tensor"
     achieved = per_launch / (avg_launch_ms / 1e3) / scale
     achieved_isolated = per_launch / (launch_ms / 1e3) / scale
     traffic = traffic_per_launch(f"config{cfg.cid}_m{m}")
 
-    # End-to-end through the public operator with pinned host buffers.
+    # Other configs, measured in this same run (N=1: configs 2, 4, 5 on both
+    # fp32 paths, 6, 7; N>1: config 3 with the all-gather over both
+    # transports, and config 5 M-sharded).
+    sub = {}
+    if args.sub != "none" and args.rows is None:
+        if world == 1:
+            for cid in (2, 4, 6, 7):
+                sub[f"config{cid}"] = sub_workload(cid, timer, P, args, device, world, rank)
+            sub["config5_tf32x3"] = sub_workload(5, timer, P, args, device, world, rank, path="tc")
+            sub["config5_simt"] = sub_workload(5, timer, P, args, device, world, rank, path="simt", steps=3)
+        else:
+            c3 = CONFIGS[3]
+            if c3.M % world == 0:
+                for tr in ("nccl", "nvlink"):
+                    try:
+                        sub[f"gathered_{tr}"] = gathered_record(c3, tr, timer, P, args, device, world, rank)
+                    except Exception as ex:  # reported, never hidden
+                        sub[f"gathered_{tr}"] = {"error": repr(ex)[:300]}
+            sub["config5_sharded_tf32x3"] = sub_workload(5, timer, P, args, device, world, rank, path="tc",
+                                                         sharded=True)
+
+    # End-to-end through the public API with pinned host buffers: host_matmul
+    # at N=1; at N>1 sharded_host_matmul (B uploaded once per job in 1/N
+    # slices and all-gathered over NVLink, each rank's A rows in, its C rows out).
     e2e = None
     if not args.no_e2e:
         hA = A.cpu().pin_memory()
         hB = B.cpu().pin_memory()
         hC = torch.empty((m, cfg.N), dtype=cfg.dtype).pin_memory()
         e_steps = max(3, min(args.steps, 10))
+        if world == 1:
+            from cmp_ext_b200.host import host_matmul
 
-        from cmp_ext_b200.host import host_matmul
+            def e2e_step():
+                host_matmul(hA, hB, out=hC, chunks=8, device=device)
+            api = "cmp_ext_b200.host.host_matmul (pinned host in/out, 8 row chunks)"
+            h2d = (hA.numel() + hB.numel()) * e
+        else:
+            from cmp_ext_b200.distributed import sharded_host_matmul
 
-        def e2e_step():
-            # host in, host out; uploads, GEMMs and downloads overlapped in row chunks
-            host_matmul(hA, hB, out=hC, chunks=8, device=device)
-
+            def e2e_step():
+                sharded_host_matmul(hA, hB, out=hC, chunks=8, device=device)
+            api = ("cmp_ext_b200.distributed.sharded_host_matmul (pinned host in/out; each rank uploads its A rows "
+                   "and 1/N of B, B all-gathered over NVLink)")
+            h2d = (hA.numel() + (hB.numel() // world if cfg.K % world == 0 else hB.numel())) * e
         for _ in range(2):
             e2e_step()
         torch.cuda.synchronize()
         barrier(world)
+        stream = torch.cuda.current_stream()
         x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         x0.record(stream)
         for _ in range(e_steps):
@@ -427,11 +682,10 @@ def run_ours(args):
         x1.record(stream)
         torch.cuda.synchronize()
         e_ms = max_over_ranks(x0.elapsed_time(x1), world, device) / e_steps
-        h2d = (hA.numel() + hB.numel()) * e
         d2h = hC.numel() * e
         ev = (step_bytes_job / (e_ms / 1e3) / 1e9) if unit == "GB/s" else (step_flops / (e_ms / 1e3) / 1e12)
         e2e = {"value": ev, "unit": unit, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-               "ms_per_step": e_ms, "api": "cmp_ext_b200.host.host_matmul (pinned host in/out, 8 row chunks)"}
+               "ms_per_step": e_ms, "api": api}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -449,20 +703,26 @@ def run_ours(args):
             cpu["torch_cpu"] = {"error": str(ex)}
 
     if rank == 0:
+        n_launch = args.steps * launches_per_step(cfg, args.rows)
         line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": cfg.dtype_name, "data": "synthetic (seeded, drawn on device)",
                 "config": {**config_block(cfg, world, gather, args.transport),
+                           "power_state": f"{args.hold:.0f} s of back-to-back steps before every timed region",
                            **({"f32_path": args.f32_path} if cfg.dtype == torch.float32 else {})},
                 "roofline": {"bound": rbound, "kernel": kernel_name(cfg, m), "achieved": achieved, "peak": peak,
                              "peak_source": peak_src, "unit": runit, "frac": achieved / peak,
                              "traffic": traffic, "launch_ms": avg_launch_ms, "timing": timing,
                              "peak_kind": peak_kind,
+                             "tflops_per_mhz": (achieved / clocks["sm_mhz"]) if (clocks and runit == "TFLOP/s")
+                             else None,
                              "isolated_launch": {"ms": launch_ms, "achieved": achieved_isolated,
                                                  "peak": peak_isolated, "frac": achieved_isolated / peak_isolated},
                              "per_launch": per_launch},
-                "e2e": e2e, "gpu_launches": args.steps * launches_per_step(cfg, args.rows),
+                "err_vs_fp64_rows": err,
+                "e2e": e2e, "gpu_launches": n_launch,
                 "clocks": clocks, "cpu_baseline": cpu,
+                "sub": sub or None,
                 "step_ms_including_flush": ms_total / args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -489,6 +749,10 @@ def main(argv=None):
     ap.add_argument("--rows", type=int, default=None, help="override this rank's M rows (profiling small cases)")
     ap.add_argument("--f32-path", default="tf32x3", choices=["tf32x3", "bf16x3"],
                     help="fp32 configs: 3xTF32 (default) or the opt-in bf16x3 split")
+    ap.add_argument("--hold", type=float, default=3.0,
+                    help="seconds of back-to-back steps before each timed region (same power state at every N)")
+    ap.add_argument("--sub", default="all", choices=["all", "none"],
+                    help="also measure the other configs in this run (N=1) / the gathered and fp32 lines (N>1)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)

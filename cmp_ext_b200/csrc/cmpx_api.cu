@@ -433,15 +433,16 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   const bool b_nmajor = bf && !g.b_kmajor && g.N % 8 == 0 && g.ldb % 4 == 0 && aligned16(g.B) &&
                         (g.batch <= 1 || g.sb % 4 == 0);
   if (bf) {
-    e = launch_split_bf16(fA, a_hi, a_lo, a_batch, g.M, g.K, g.lda, g.sa, false, s);
+    e = launch_split_bf16(fA, a_hi, a_lo, a_batch, g.M, g.K, g.lda, g.sa, false, d->info.num_sms, s);
     if (e == cudaSuccess)
-      e = launch_split_bf16(fB, b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb, !g.b_kmajor && !b_nmajor, s);
+      e = launch_split_bf16(fB, b_hi, b_lo, g.batch, b_rows, b_cols, g.ldb, g.sb, !g.b_kmajor && !b_nmajor,
+                            d->info.num_sms, s);
   } else {
     e = launch_split_tf32(fA, static_cast<float*>(a_hi), static_cast<float*>(a_lo), a_batch, g.M, g.K, g.lda, g.sa,
-                          false, s);
+                          false, d->info.num_sms, s);
     if (e == cudaSuccess)
       e = launch_split_tf32(fB, static_cast<float*>(b_hi), static_cast<float*>(b_lo), g.batch, b_rows, b_cols, g.ldb,
-                            g.sb, !g.b_kmajor, s);
+                            g.sb, !g.b_kmajor, d->info.num_sms, s);
   }
   if (e != cudaSuccess) return CMPX_ERR_CUDA;
   CUtensorMap tA, tA2, tB, tB2;

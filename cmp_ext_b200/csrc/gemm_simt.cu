@@ -104,12 +104,16 @@ __global__ void fill_bias_kernel(T* __restrict__ C, const T* __restrict__ bias, 
   }
 }
 
+// C[r, c] += bias[c]: blockIdx.x / threadIdx.x pick the column (the bias
+// value stays in a register), blockIdx.y strides over rows; no index division.
 template <typename T>
 __global__ void add_bias_kernel(T* __restrict__ C, const T* __restrict__ bias, long long rows, long long cols) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < rows * cols;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long c = i % cols;
-    st_f32(C + i, ld_f32(C + i) + ld_f32(bias + c));
+  const long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const float b = ld_f32(bias + c);
+  for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
+    T* p = C + r * cols + c;
+    st_f32(p, ld_f32(p) + b);
   }
 }
 
@@ -135,11 +139,14 @@ cudaError_t fill_t(const Gemm& g, cudaStream_t s) {
 
 template <typename T>
 cudaError_t bias_t(void* C, const void* bias, int64_t rows, int64_t cols, cudaStream_t s) {
-  long long blocks = (rows * cols + 255) / 256;
-  if (blocks > 4096) blocks = 4096;
-  if (blocks < 1) blocks = 1;
-  add_bias_kernel<T><<<unsigned(blocks), 256, 0, s>>>(reinterpret_cast<T*>(C), reinterpret_cast<const T*>(bias), rows,
-                                                       cols);
+  const long long bx = (cols + 255) / 256;
+  if (bx > 0x7fffffffLL) return cudaErrorInvalidValue;
+  long long by = (8192 + bx - 1) / bx;  // about 8192 blocks in all
+  if (by > rows) by = rows;
+  if (by > 65535) by = 65535;
+  if (by < 1) by = 1;
+  add_bias_kernel<T><<<dim3(unsigned(bx), unsigned(by)), 256, 0, s>>>(reinterpret_cast<T*>(C),
+                                                                      reinterpret_cast<const T*>(bias), rows, cols);
   return cudaGetLastError();
 }
 

@@ -546,12 +546,19 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
+// hi is rounded to nearest, so a finite x within half an ulp of the format's
+// largest finite value would round hi to infinity (and lo to -infinity),
+// where the reference's fp32 arithmetic stays finite.  hi is then clamped to
+// the largest finite value of the format, with x's sign, and lo carries the
+// (small, exactly representable) rest.
 __device__ __forceinline__ void split1(float x, float& h, float& l) {
   h = tf32_rna(x);
+  if (isinf(h) && !isinf(x)) h = copysignf(__uint_as_float(0x7F7FE000u), x);  // largest finite tf32
   l = tf32_rna(x - h);
 }
 __device__ __forceinline__ void split1(float x, __nv_bfloat16& h, __nv_bfloat16& l) {
   h = __float2bfloat16_rn(x);
+  if (__hisinf(h) && !isinf(x)) h = __ushort_as_bfloat16(x < 0.0f ? 0xFF7Fu : 0x7F7Fu);  // largest finite bf16
   l = __float2bfloat16_rn(x - __bfloat162float(h));
 }
 
@@ -577,11 +584,13 @@ struct Vec4<__nv_bfloat16> {
 };
 
 // X [rows][cols] (row stride ld) -> packed hi, lo [rows][cols].  Vector
-// form: cols % 4 == 0, ld % 4 == 0 and X 16-byte aligned.  Blocks stride over
-// rows and threads over a row's float4s, so no index needs a division.
+// form: cols % 4 == 0, ld % 4 == 0 and X 16-byte aligned.  A block holds
+// 256 >> tpr_log2 rows of 1 << tpr_log2 threads each (a power of two >= the
+// row's float4 count, at most 256), so short rows still keep every thread
+// busy; blocks stride over row groups and no index needs a division.
 template <typename S>
 __global__ void split_vec_kernel(const float* __restrict__ X, S* __restrict__ hi, S* __restrict__ lo,
-                                 long long rows, long long cols, long long ld, long long sx) {
+                                 long long rows, long long cols, long long ld, long long sx, int tpr_log2) {
   pdl_trigger();
   pdl_wait();  // X may be the previous kernel's output
   const long long b = blockIdx.y;
@@ -589,11 +598,15 @@ __global__ void split_vec_kernel(const float* __restrict__ X, S* __restrict__ hi
   const float* xb = X + b * sx;
   S* hb = hi + b * rows * cols;
   S* lb = lo + b * rows * cols;
-  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+  const int tpr = 1 << tpr_log2;
+  const int sub = threadIdx.x >> tpr_log2;
+  const int lane_r = threadIdx.x & (tpr - 1);
+  const long long rpb = blockDim.x >> tpr_log2;
+  for (long long r = blockIdx.x * rpb + sub; r < rows; r += gridDim.x * rpb) {
     const float4* xr = reinterpret_cast<const float4*>(xb + r * ld);
     S* hr = hb + r * cols;
     S* lr = lb + r * cols;
-    for (long long c = threadIdx.x; c < c4; c += blockDim.x) {
+    for (long long c = lane_r; c < c4; c += tpr) {
       const float4 x = __ldcs(xr + c);
       Vec4<S> h, l;
 #pragma unroll
@@ -687,7 +700,7 @@ cudaError_t launch_plain_pdl(void (*kern)(KArgs...), dim3 grid, cudaStream_t s, 
 namespace {
 template <typename S>
 cudaError_t launch_split_impl(const float* X, S* hi, S* lo, int64_t batch, int64_t rows, int64_t cols, int64_t ld,
-                              int64_t sx, bool transpose, cudaStream_t s) {
+                              int64_t sx, bool transpose, int num_sms, cudaStream_t s) {
   const bool vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && cols % 4 == 0 && ld % 4 == 0 &&
                    (batch <= 1 || sx % 4 == 0);
   if (transpose) {
@@ -698,14 +711,19 @@ cudaError_t launch_split_impl(const float* X, S* hi, S* lo, int64_t batch, int64
     return launch_plain_pdl(split_transpose_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
   }
   if (vec) {
-    // one block per row (up to 16 per SM resident), grid-strided beyond that
-    const long long blocks = rows < 148 * 16 ? (rows > 0 ? rows : 1) : 148 * 16;
+    int tpr_log2 = 0;
+    while (tpr_log2 < 8 && (1LL << tpr_log2) < cols / 4) ++tpr_log2;
+    const long long rpb = 256 >> tpr_log2;
+    // a block per row group, up to 8 resident 256-thread blocks per SM; grid-strided beyond that
+    long long blocks = (rows + rpb - 1) / rpb;
+    if (blocks > 8LL * num_sms) blocks = 8LL * num_sms;
+    if (blocks < 1) blocks = 1;
     const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
-    return launch_plain_pdl(split_vec_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
+    return launch_plain_pdl(split_vec_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx, tpr_log2);
   }
   const long long n = rows * cols;
   long long blocks = (n + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks > 8LL * num_sms) blocks = 8LL * num_sms;
   if (blocks < 1) blocks = 1;
   const dim3 grid{unsigned(blocks), unsigned(batch), 1u};
   return launch_plain_pdl(split_kernel<S>, grid, s, X, hi, lo, rows, cols, ld, sx);
@@ -713,14 +731,14 @@ cudaError_t launch_split_impl(const float* X, S* hi, S* lo, int64_t batch, int64
 }  // namespace
 
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
-                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
-  return launch_split_impl<float>(X, hi, lo, batch, rows, cols, ld, sx, transpose, s);
+                              int64_t ld, int64_t sx, bool transpose, int num_sms, cudaStream_t s) {
+  return launch_split_impl<float>(X, hi, lo, batch, rows, cols, ld, sx, transpose, num_sms, s);
 }
 
 cudaError_t launch_split_bf16(const float* X, void* hi, void* lo, int64_t batch, int64_t rows, int64_t cols,
-                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s) {
+                              int64_t ld, int64_t sx, bool transpose, int num_sms, cudaStream_t s) {
   return launch_split_impl<__nv_bfloat16>(X, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), batch,
-                                          rows, cols, ld, sx, transpose, s);
+                                          rows, cols, ld, sx, transpose, num_sms, s);
 }
 
 }  // namespace cmpx

@@ -87,10 +87,10 @@ cudaError_t launch_tc_bf16x3(const Gemm& g, const CUtensorMap& tA, const CUtenso
 // packed tf32 hi and lo parts: [batch][rows][cols] contiguous, or with
 // transpose = true [batch][cols][rows] contiguous.
 cudaError_t launch_split_tf32(const float* X, float* hi, float* lo, int64_t batch, int64_t rows, int64_t cols,
-                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s);
+                              int64_t ld, int64_t sx, bool transpose, int num_sms, cudaStream_t s);
 // The same with bf16 hi = rn(x), lo = rn(x - hi) (hi, lo: __nv_bfloat16).
 cudaError_t launch_split_bf16(const float* X, void* hi, void* lo, int64_t batch, int64_t rows, int64_t cols,
-                              int64_t ld, int64_t sx, bool transpose, cudaStream_t s);
+                              int64_t ld, int64_t sx, bool transpose, int num_sms, cudaStream_t s);
 
 // Swap-AB stream-K kernel for skinny M (M <= 128), fp16/bf16.
 // tBop maps B as the MMA's 128-row operand, tAop maps A as the MMA's

@@ -65,18 +65,25 @@ def _draw(shape, dist: str, std: float, gen: torch.Generator, device) -> torch.T
 
 
 def make_inputs(cfg: Config, device="cpu", seed: int = 0, rows: tuple[int, int] | None = None,
-                m: int | None = None):
+                m: int | None = None, a_seed: int | None = None):
     """Seeded A [M,K] and B [K,N] of cfg.dtype on `device`.
 
     The draw happens on `device` with a generator seeded by `seed` (so a CPU
     draw and a CUDA draw differ, but each is reproducible).  `rows` returns
     only A[r0:r1] (the rows an M-shard owns) with the same values the full
-    draw would have; `m` overrides cfg.M.
+    draw would have; `m` overrides cfg.M.  With `a_seed`, B is drawn from
+    `seed` alone and A from its own generator seeded `a_seed` (M-sharded
+    runs: the same B on every rank, a different A shard per rank).
     """
     M = cfg.M if m is None else m
     gen = torch.Generator(device=device).manual_seed(seed)
+    b_dist = cfg.a_dist if cfg.a_dist == "uniform" else "normal"
+    if a_seed is not None:
+        B = _draw((cfg.K, cfg.N), b_dist, cfg.b_std, gen, device)
+        A = _draw((M, cfg.K), cfg.a_dist, 1.0, torch.Generator(device=device).manual_seed(a_seed), device)
+        return A.to(cfg.dtype), B.to(cfg.dtype)
     A = _draw((M, cfg.K), cfg.a_dist, 1.0, gen, device)
-    B = _draw((cfg.K, cfg.N), cfg.a_dist if cfg.a_dist == "uniform" else "normal", cfg.b_std, gen, device)
+    B = _draw((cfg.K, cfg.N), b_dist, cfg.b_std, gen, device)
     if rows is not None:
         A = A[rows[0]:rows[1]].contiguous()
     return A.to(cfg.dtype), B.to(cfg.dtype)

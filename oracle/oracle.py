@@ -29,12 +29,30 @@ _lib = None
 _ref = None
 
 
+def reference_dir() -> str | None:
+    """The reference checkout: $CMPX_REFERENCE_DIR, else BASELINE.json's
+    `reference_path` at the repository root; None when neither names an
+    existing directory (e.g. on a GPU box, which uses the prebuilt _ref)."""
+    d = os.environ.get("CMPX_REFERENCE_DIR")
+    if not d:
+        try:
+            import json
+
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                d = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            d = None
+    return d if d and os.path.isdir(d) else None
+
+
 def build(force: bool = False) -> None:
     """Compiles liboracle.so (and oracle/_ref when the reference sources exist)."""
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(os.path.join(HERE, "ref_matmul.c")):
         subprocess.run(["make", "-s", "-f", os.path.join(HERE, "Makefile"), LIB], check=True)
-    subprocess.run(["make", "-s", "-f", os.path.join(HERE, "Makefile"), "ref"], check=True,
-                   stdout=subprocess.DEVNULL)
+    ref = reference_dir()
+    if ref is not None:
+        subprocess.run(["make", "-s", "-f", os.path.join(HERE, "Makefile"), f"REF={ref}", "ref"], check=True,
+                       stdout=subprocess.DEVNULL)
 
 
 def _load():

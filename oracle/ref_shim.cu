@@ -1,8 +1,8 @@
 // ref_shim.cu -- extern "C" entry points over the reference's own launchers.
 //
 // TEST INFRASTRUCTURE ONLY.  Linked together with the reference's unmodified
-// src/cuda/{fp16,fp32,bf16}_matmul.cu (compiled from /root/reference by
-// oracle/Makefile into oracle/_ref/libref_matmul.so) so the GPU parity tests
+// src/cuda/{fp16,fp32,bf16}_matmul.cu (compiled from the reference checkout
+// named by REF by oracle/Makefile into oracle/_ref/libref_matmul.so) so the GPU parity tests
 // can run the reference kernel itself on the B200 as a second oracle.  The
 // launcher prototypes are the reference's (src/main.cpp:12-19).
 #include <cuda_runtime.h>

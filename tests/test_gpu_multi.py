@@ -1,8 +1,10 @@
-"""M-sharded matmul on two GPUs (one process per GPU, launched as child
-processes).  Skipped on a one-GPU box.  Checks that every rank ends up with
-the full product -- NCCL in-place gather, NCCL chunked gather, and the fused
-NVLink epilogue stores into symmetric memory -- equal to the product one GPU
-computes."""
+"""M-sharded matmul with one process per GPU, launched as child processes:
+on two GPUs (skipped on a one-GPU box) and as a one-rank job (runs on any
+box, so the collective plumbing runs on every GPU test pass).  Checks that
+every rank ends up with the full product -- NCCL in-place gather, NCCL
+chunked gather, and the fused NVLink epilogue stores into symmetric memory --
+equal to the product one GPU computes, and that the host-to-host sharded
+matmul (B uploaded in slices and all-gathered) gives each rank its rows."""
 import os
 import socket
 import subprocess
@@ -46,6 +48,15 @@ for rep in range(2):
     assert not torch.isnan(C.float()).any(), "nvlink gather left rows unwritten"
     err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
     assert err <= 2 ** -7, ("nvlink", err)
+from cmp_ext_b200.distributed import sharded_host_matmul
+hA = A[r0:r1].cpu().pin_memory()
+hB = B.cpu().pin_memory()
+for K_cut in (K, K - 1):  # K % world == 0 (slices gathered) and, at 2 ranks, ragged K (full upload)
+    hC = sharded_host_matmul(hA[:, :K_cut].contiguous(), hB[:K_cut].contiguous(), chunks=3)
+    torch.cuda.synchronize()
+    want = cx.bf16_matmul(A[r0:r1, :K_cut].contiguous(), B[:K_cut].contiguous()).cpu()
+    err = ((hC.float() - want.float()).abs().max() / want.float().abs().max()).item()
+    assert err <= 2 ** -7, ("host", K_cut, err)
 mine = sharded_matmul(A[r0:r1].contiguous(), B)
 assert torch.equal(mine, full[r0:r1]) or ((mine.float() - full[r0:r1].float()).abs().max() / full.float().abs().max()).item() <= 2 ** -7
 dist.barrier()
@@ -62,14 +73,15 @@ def _port():
     return p
 
 
-def test_sharded_gather_two_gpus(cuda, tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [1, 2])
+def test_sharded_gather(cuda, tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     script = tmp_path / "worker.py"
     script.write_text(WORKER)
     env = dict(os.environ, REPO=REPO, NCCL_NVLS_ENABLE="0")
-    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
                         "--master-addr=127.0.0.1", f"--master-port={_port()}", str(script)],
                        env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
-    assert r.stdout.count(" ok") == 2
+    assert r.stdout.count(" ok") == world

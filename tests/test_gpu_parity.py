@@ -177,6 +177,33 @@ def test_bf16x3_workspace_and_odd_k(cuda):
     run_cabi(A2, B2, path=cabi.PATH_BF16X3, expect=cabi.ERR_UNSUPPORTED)
 
 
+@pytest.mark.parametrize("path", [cabi.PATH_TC, cabi.PATH_BF16X3])
+@pytest.mark.parametrize("b_layout", [cabi.B_KN, cabi.B_NK])
+def test_f32_split_near_flt_max(cuda, path, b_layout):
+    """fp32 inputs within half an ulp (of tf32 / bf16) of FLT_MAX: rounding
+    the hi part to nearest would give inf and lo = -inf, so the product would
+    be NaN where the reference's fp32 arithmetic is finite.  hi is clamped to
+    the format's largest finite value; the result must match the oracle's
+    error bound like any other input."""
+    M, N, K = 256, 264, 136
+    g = torch.Generator().manual_seed(21)
+    fmax = torch.finfo(torch.float32).max
+    A = (torch.rand(M, K, generator=g) * 0.02 + 0.98) * fmax
+    A = torch.where(torch.rand(M, K, generator=g) < 0.5, A, -A)
+    A[0, :] = fmax
+    A[1, :] = -fmax
+    A[2, ::2] = torch.tensor(0x7F7FF000, dtype=torch.int32).view(torch.float32)  # rounds up in tf32 and bf16
+    B = torch.randn(K, N, generator=g) * 2.0 ** -100  # products ~2^28: no overflow in any partial sum
+    Bdev = (B if b_layout == cabi.B_KN else B.t().contiguous()).cuda()
+    C = run_cabi(A.cuda(), Bdev, b_layout=b_layout, path=path)
+    assert torch.isfinite(C).all()
+    C64 = o.fp64_matmul("f32", A.numpy(), B.numpy())
+    ref = o.oracle_matmul("f32", A.numpy(), B.numpy())
+    err = o.normwise_err(C.double().cpu().numpy(), C64)
+    ref_err = o.normwise_err(ref.astype(np.float64), C64)
+    assert err <= ref_err + TOL[torch.float32], (err, ref_err)
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("shape", [(257, 383, 511), (5, 7, 3), (70, 130, 33), (1, 1, 1)],
                          ids=lambda s: "x".join(map(str, s)))

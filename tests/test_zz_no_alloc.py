@@ -44,6 +44,9 @@ def test_noalloc_matches_gemm_twice(cuda, dtype, M, N, K, layout, bias):
     Bshape = (K, N) if layout == cabi.B_KN else (N, K)
     B = (torch.randn(Bshape, generator=g, device="cuda") * 0.02).to(dtype)
     bvec = torch.randn(N, generator=g, device="cuda").to(dtype) if bias else None
+    # fp64 ground truth of the same product (exact inputs, fp64 accumulation)
+    Bkn = B if layout == cabi.B_KN else B.t()
+    C64 = (A.double() @ Bkn.double() + (bvec.double()[None, :] if bias else 0)).cpu().numpy()
     ref = torch.empty((M, N), dtype=dtype, device="cuda")
     args = cabi.gemm_args(A, B, ref, bias=bvec, b_layout=layout, path=cabi.PATH_SKINNY)
     assert cabi.gemm(args, torch.cuda.current_stream().cuda_stream) == cabi.OK
@@ -53,6 +56,12 @@ def test_noalloc_matches_gemm_twice(cuda, dtype, M, N, K, layout, bias):
         assert st == cabi.OK, cabi.lib().cmpx_status_string(st)
         torch.cuda.synchronize()
         assert not torch.isnan(C.float()).any()
+        # the path's contract against fp64: err <= err(reference kernel) + 1e-3,
+        # checked here against the stricter 1e-3 alone
+        err64 = o.normwise_err(C.double().cpu().numpy(), C64)
+        assert err64 <= 1e-3, err64
+        # and the same numbers as cmpx_gemm's skinny path (same kernel, its
+        # scratch from the library workspace instead of the fixed array)
         err = o.normwise_err(C.double().cpu().numpy(), ref.double().cpu().numpy())
         assert err <= 1e-3, err
     assert cabi.device_error() == 0

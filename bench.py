@@ -360,20 +360,9 @@ class Timer:
             torch.cuda.synchronize()
             n = min(n * 2, 64)
 
-    def run(self, step, steps, warmup, flush=None):
-        """(ms of the K steps minus their L2 flushes, clocks)."""
+    def run(self, step, steps, warmup):
+        """(ms of the K back-to-back steps, max over ranks; clocks)."""
         self.hold(step, warmup)
-        flush_ms = 0.0
-        if flush is not None:
-            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            f0.record(self.stream)
-            for _ in range(steps):
-                flush.fill_(1)
-            f1.record(self.stream)
-            torch.cuda.synchronize()
-            flush_ms = f0.elapsed_time(f1)
-            for _ in range(3):
-                step()
         barrier(self.world)
         torch.cuda.synchronize()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -381,31 +370,41 @@ class Timer:
             self.clock.start()
         ev0.record(self.stream)
         for _ in range(steps):
-            if flush is not None:
-                flush.fill_(1)
             step()
         ev1.record(self.stream)
         torch.cuda.synchronize()
         clocks = self.clock.stop() if self.clock is not None else None
         barrier(self.world)
-        ms = max(ev0.elapsed_time(ev1) - flush_ms, 1e-6)
+        ms = ev0.elapsed_time(ev1)
         return max_over_ranks(ms, self.world, self.device), clocks
 
-    def isolated(self, fn, reps, flush=None):
-        """Median event time of single launches with the GPU idle around each."""
+    def isolated(self, fn, reps):
+        """Median event time of single launches, each after a device sync."""
         k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         out = []
         for _ in range(reps):
-            if flush is not None:
-                flush.fill_(1)
             torch.cuda.synchronize()
-            time.sleep(0.002)
             k0.record(self.stream)
             fn()
             k1.record(self.stream)
             torch.cuda.synchronize()
             out.append(k0.elapsed_time(k1))
         return statistics.median(out)
+
+
+L2_BYTES = 126e6
+
+
+def input_sets(cfg, device, m, rank):
+    """Resident input sets for one workload: enough of them that the sets a
+    step cycles through exceed three times the L2 (126 MB), so consecutive
+    steps never find their operands in L2 and no flush is needed."""
+    n = max(1, min(16, int(-(-3 * L2_BYTES // cfg.bytes(m))))) if cfg.bytes(m) < 3 * L2_BYTES else 1
+    sets = [make_inputs(cfg, device, seed=0 if i == 0 else 7 + i, m=m, a_seed=1000 + rank + 64 * i)
+            for i in range(n)]
+    desc = ("inputs larger than L2 (126 MB) per GPU" if n == 1 else
+            f"{n} resident input sets rotated per step ({n * cfg.bytes(m) / 1e6:.0f} MB > 3 x L2); no flush")
+    return sets, desc
 
 
 def rows_err(C, A, B, rows=64):
@@ -459,27 +458,27 @@ def sub_workload(cid, timer, P, args, device, world, rank, path=None, steps=None
     cfg = CONFIGS[cid]
     r0, r1 = shard_rows(cfg.M, world, rank) if sharded else (0, cfg.M)
     m = r1 - r0
-    A, B = make_inputs(cfg, device, seed=0, m=m, a_seed=1000 + rank)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device) if cfg.bytes(m) <= 189e6 else None
+    sets, l2 = input_sets(cfg, device, m, rank)
     op = op_for(cfg.dtype)
     prev = None
     if path is not None:
         ext._set_path(path)
     try:
-        out = {}
+        out = {"i": 0}
 
         def step():
-            out["C"] = op(A, B)
+            A, B = sets[out["i"] % len(sets)]
+            out["i"] += 1
+            out["C"], out["AB"] = op(A, B), (A, B)
 
         K = steps or max(3, min(args.steps, 20))
-        ms, clocks = timer.run(step, K, 3, flush)
-        launch_ms = timer.isolated(step, 5 if K >= 5 else 2, flush)
-        err = rows_err(out["C"], A, B)
+        ms, clocks = timer.run(step, K, 3)
+        launch_ms = timer.isolated(step, 5 if K >= 5 else 2)
+        err = rows_err(out["C"], *out["AB"])
         kern = kernel_name(cfg, m) if path is None else {"simt": "gemm_simt_kernel", "tc": kernel_name(cfg, m),
                                                          "bf16x3": "gemm_tc_kernel(bf16x3)"}[path]
         rec = tensor_record(cfg, m, ms / K, clocks, P, kern, launch_ms,
-                            {"err_vs_fp64_rows": err, "steps": K, "l2": "flushed" if flush is not None else
-                             "inputs larger than L2"})
+                            {"err_vs_fp64_rows": err, "steps": K, "l2": l2})
         if sharded:
             job = 2.0 * cfg.M * cfg.N * cfg.K
             rec["job_value"] = job / (ms / K / 1e3) / 1e12
@@ -495,7 +494,8 @@ def sub_workload(cid, timer, P, args, device, world, rank, path=None, steps=None
     finally:
         if path is not None:
             ext._set_path(prev or "auto")
-        del A, B
+        sets.clear()
+        out.clear()
         torch.cuda.empty_cache()
 
 
@@ -508,7 +508,7 @@ def gathered_record(cfg, transport, timer, P, args, device, world, rank):
 
     S = cfg.M // world
     A, B = make_inputs(cfg, device, seed=0, m=S, a_seed=1000 + rank)
-    if transport == "nvlink":
+    if transport in ("nvlink", "ce"):
         Cfull = gather_output(cfg.M, cfg.N, cfg.dtype, device)
     else:
         Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
@@ -543,6 +543,7 @@ def gathered_record(cfg, transport, timer, P, args, device, world, rank):
 
 
 def run_ours(args):
+    sys.setswitchinterval(0.0005)  # let the clock-sampling thread run while this one launches
     world, rank, local = dist_setup(args)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -562,33 +563,33 @@ def run_ours(args):
     timer = Timer(world, device, args.quick, args.hold)
 
     # Inputs resident in HBM (drawn on the device; the same B on every rank,
-    # a different A shard per rank).
-    A, B = make_inputs(cfg, device, seed=0, m=m, a_seed=1000 + rank)
-    A = A.contiguous()
-    flush = None
-    if cfg.bytes(m) <= 126e6 * 1.5:
-        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)  # 256 MB > L2
+    # a different A shard per rank; small configs rotate several sets so the
+    # operands of a step are never in L2).
+    sets, l2_desc = input_sets(cfg, device, m, rank)
+    A, B = sets[0]
 
     gather = args.gather and world > 1
     if gather:
         from cmp_ext_b200.distributed import gather_output, sharded_matmul
-        if args.transport == "nvlink":
+        if args.transport in ("nvlink", "ce"):
             Cfull = gather_output(cfg.M, cfg.N, cfg.dtype, device)
         else:
             Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
 
-    last = {}
+    last = {"i": 0}
 
     def step():
         if gather:
             sharded_matmul(A, B, M=cfg.M, gather=True, chunks=args.chunks, out=Cfull, transport=args.transport)
         else:
-            last["C"] = op(A, B)
+            a, b = sets[last["i"] % len(sets)]
+            last["i"] += 1
+            last["C"], last["AB"] = op(a, b), (a, b)
 
-    ms_gemm, clocks = timer.run(step, args.steps, args.warmup if args.quick else max(3, args.warmup), flush)
-    ms_total = ms_gemm
-    launch_ms = timer.isolated(lambda: op(A, B), 1 if args.quick else max(5, min(args.steps, 20)), flush)
-    err = None if gather or args.quick else rows_err(last["C"], A, B)
+    ms_gemm, clocks = timer.run(step, args.steps, args.warmup if args.quick else max(3, args.warmup))
+    launch_ms = timer.isolated(step if not gather else (lambda: op(A, B)),
+                               1 if args.quick else max(5, min(args.steps, 20)))
+    err = None if gather or args.quick else rows_err(last["C"], *last["AB"])
 
     M_job = cfg.M if args.rows is None else args.rows * world
     step_flops = 2.0 * M_job * cfg.N * cfg.K  # whole job (all ranks)
@@ -605,7 +606,7 @@ def run_ours(args):
     # otherwise the isolated launch.
     one_launch = launches_per_step(cfg, args.rows) == 1 and not gather
     avg_launch_ms = ms_per_step if one_launch else launch_ms
-    timing = ("timed region / K (back-to-back launches, L2 flush time subtracted)" if one_launch
+    timing = ("timed region / K (back-to-back launches)" if one_launch
               else "median of isolated launches (events around each)")
     scale = 1e9 if cfg.bound == "hbm" else 1e12
     if cfg.bound == "hbm":
@@ -638,7 +639,7 @@ def run_ours(args):
         else:
             c3 = CONFIGS[3]
             if c3.M % world == 0:
-                for tr in ("nccl", "nvlink"):
+                for tr in ("nccl", "nvlink", "ce"):
                     try:
                         sub[f"gathered_{tr}"] = gathered_record(c3, tr, timer, P, args, device, world, rank)
                     except Exception as ex:  # reported, never hidden
@@ -707,7 +708,7 @@ def run_ours(args):
         line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": cfg.dtype_name, "data": "synthetic (seeded, drawn on device)",
-                "config": {**config_block(cfg, world, gather, args.transport),
+                "config": {**config_block(cfg, world, gather, args.transport), "l2": l2_desc,
                            "power_state": f"{args.hold:.0f} s of back-to-back steps before every timed region",
                            **({"f32_path": args.f32_path} if cfg.dtype == torch.float32 else {})},
                 "roofline": {"bound": rbound, "kernel": kernel_name(cfg, m), "achieved": achieved, "peak": peak,
@@ -722,8 +723,7 @@ def run_ours(args):
                 "err_vs_fp64_rows": err,
                 "e2e": e2e, "gpu_launches": n_launch,
                 "clocks": clocks, "cpu_baseline": cpu,
-                "sub": sub or None,
-                "step_ms_including_flush": ms_total / args.steps}
+                "sub": sub or None}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -740,8 +740,9 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="all-gather C to every rank (N>1)")
     ap.add_argument("--chunks", type=int, default=1, help="row chunks for the overlapped gather (1 = in place)")
-    ap.add_argument("--transport", default="nccl", choices=["nccl", "nvlink"],
-                    help="gather: NCCL all-gather, or epilogue stores into peers' outputs over NVLink")
+    ap.add_argument("--transport", default="nccl", choices=["nccl", "nvlink", "ce"],
+                    help="gather: NCCL all-gather, epilogue stores into peers' outputs over NVLink, or copy-engine "
+                         "copies of finished tile columns")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true",

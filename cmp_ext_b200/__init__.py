@@ -24,7 +24,7 @@ import torch  # noqa: F401  (loads libtorch / c10 before the shim)
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcmpx.so")
 
-_OPS = ("linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul", "_set_path", "_matmul_into", "version")
+_OPS = ("linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul", "_set_path", "_matmul_into", "_matmul_gather_ce", "version")
 
 
 def _load_ext():

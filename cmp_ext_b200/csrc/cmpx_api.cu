@@ -483,6 +483,30 @@ int packed_matmul(int dtype, const void* A, const void* B, void* C, int64_t M, i
 
 }  // namespace
 
+// The CTA-pair GEMM with column-progress flags (gather_ce.cu): fp16/bf16,
+// one 256-column pair-tile kernel launch, whole tiles only (every tile
+// counts into its flag), no peer stores.
+int run_gemm_flagged(const cmpx_gemm_args* args, int* flags, int flag_tiles, cudaStream_t s) {
+  int st = validate(args);
+  if (st != CMPX_OK) return st;
+  if (args->batch == 0 || args->M == 0 || args->N == 0) return CMPX_OK;
+  DeviceState* d = nullptr;
+  st = device_state(&d);
+  if (st != CMPX_OK) return st;
+  Gemm g = to_gemm(args);
+  g.col_flags = flags;
+  g.flag_tiles = flag_tiles;
+  if (g.dtype == CMPX_F32 || choose_path(g, args->path, &d->info) != CMPX_PATH_TC) return CMPX_ERR_UNSUPPORTED;
+  if (tc_pair_n(g, d->info) != 256) return CMPX_ERR_UNSUPPORTED;
+  CUtensorMap tA, tB;
+  st = encode_3d(&tA, g.dtype, g.A, g.K, g.M, g.a_bcast ? 1 : g.batch, g.lda, g.sa, 64, 128);
+  if (st != CMPX_OK) return st;
+  st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 128)
+                  : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
+  if (st != CMPX_OK) return st;
+  return cuda_status(launch_tc2_f16(g, tA, tB, 256, nullptr, d->info, d->err_word, s));
+}
+
 // CMPX_PDL=0 turns programmatic dependent launch off (A/B measurements).
 bool pdl_enabled() {
   static int on = -1;
@@ -491,6 +515,16 @@ bool pdl_enabled() {
     on = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
   return on == 1;
+}
+
+unsigned epilogue_sleep_ns() {
+  static long v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("CMPX_EPI_SLEEP_NS");
+    long x = e != nullptr ? std::strtol(e, nullptr, 10) : 0;
+    v = x < 0 ? 0 : (x > 100000 ? 100000 : x);
+  }
+  return unsigned(v);
 }
 
 int* device_error_word() {

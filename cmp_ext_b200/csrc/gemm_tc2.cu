@@ -49,6 +49,9 @@ struct Tc2Params {
   int a_bcast;
   int bias_m;
   PeerOut peers;
+  int* col_flags;  // column-progress flags (see Gemm::col_flags), nullptr = none
+  int flag_tiles;
+  unsigned epi_sleep_ns;  // epilogue's accumulator wait: sleep between polls (0 = spin)
   int* err;
 };
 
@@ -203,7 +206,10 @@ __device__ __forceinline__ void pack_row32_16(const uint32_t (&r)[32], const T* 
   }
 }
 
-template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT>
+// STREAMK: the kernel may be given split (stream-K) tiles and carries their
+// partial-sum hand-off; the default instantiation is whole tiles only, which
+// keeps the split path's 128-float reduction registers out of it.
+template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT, bool STREAMK>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const Tc2Params p, const __grid_constant__ OutMaps om) {
@@ -359,7 +365,7 @@ __global__ void __launch_bounds__(192, 1)
       decode_tile2(w.tile, p, b, tm, tn);
       const int acc = int(lt % Cfg::NACC);
       const uint32_t acc_phase = (lt / Cfg::NACC) & 1;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, abort_flag));
+      const bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(&acc_full[acc], acc_phase, abort_flag, p.epi_sleep_ns));
       if (!ok) {
         if (lane == 0) record_error2(p.err, abort_flag, kDevTimeoutAccFull);
         break;
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(192, 1)
         g_lo = sk_owner(t_u0, p.sk_units, P);
         g_hi = sk_owner(t_u0 + num_kb - 1, p.sk_units, P);
       }
-      const bool whole = w.skt < 0 || g_lo == g_hi;
+      const bool whole = !STREAMK || w.skt < 0 || g_lo == g_hi;
       float* part = nullptr;
       if (!whole) {
         const int slot = (w.skt == first_skt) ? 0 : 1;
@@ -421,8 +427,19 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       mbar_arrive_cluster(mapa_cluster(&acc_empty[acc], 0));
+      if (p.col_flags != nullptr && whole) {
+        // This warp's 32 rows of the tile are stored: one lane publishes them
+        // at system scope and counts them (8 arrivals per pair tile: 4
+        // epilogue warps x 2 CTAs), so a copy engine waiting on the flag
+        // reads finished rows.  Per warp, so no warp ever waits on another.
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence_system();
+          atomicAdd(p.col_flags + tn / p.flag_tiles, 1);
+        }
+      }
 
-      if (!whole) {
+      if (STREAMK && !whole) {
         // The last part of this split tile to arrive (per CTA half and
         // epilogue warp) sums the parts in pair order, adds the bias, rounds
         // once and stores; it then zeroes the counter for the next launch.
@@ -474,6 +491,12 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (TMA_OUT) {
     if (warp >= 2 && lane == 0) bulk_wait_all();  // staged output stores have landed
   }
+  if (p.col_flags != nullptr && threadIdx.x == 0 && *abort_flag) {
+    // A launch that gave up never completes its tiles: release every waiter
+    // on the flags (the error word tells the host the output is not valid).
+    const int groups = (p.tiles_n + p.flag_tiles - 1) / p.flag_tiles;
+    for (int j = 0; j < groups; ++j) atomicAdd(p.col_flags + j, 1 << 24);
+  }
   __syncwarp();
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still signal its barriers
@@ -483,11 +506,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT>
+template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT, bool STREAMK>
 cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
                            const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps& om) {
   using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES, TMA_OUT>;
-  auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES, TMA_OUT>;
+  auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES, TMA_OUT, STREAMK>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
   static unsigned long long smem_set = 0;  // one flag word per kernel instantiation
   cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
@@ -507,6 +530,9 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   p.a_bcast = g.a_bcast;
   p.bias_m = g.bias_m;
   p.peers = g.peers;
+  p.col_flags = g.col_flags;
+  p.flag_tiles = g.flag_tiles > 0 ? g.flag_tiles : 1;
+  p.epi_sleep_ns = epilogue_sleep_ns();
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;
   const long long pairs = dev.num_sms / 2;
@@ -516,7 +542,7 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   // is less than a wave.
   const long long rem = total % pairs;
   long long sk = 0;
-  if (ws != nullptr && rem != 0) sk = total >= pairs ? rem + pairs : total;
+  if (STREAMK && ws != nullptr && rem != 0) sk = total >= pairs ? rem + pairs : total;
   p.dp_tiles = int(total - sk);
   p.sk_tiles = int(sk);
   p.sk_units = sk * num_kb;
@@ -544,9 +570,11 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
 template <int FMT, bool B_KMAJOR, int PN, int STAGES>
 cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
                             const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om) {
-  if (om != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, true>(g, tA, tB, ws, dev, dev_err, s, *om);
+  // Peer outputs (staged TMA stores) run whole tiles only.
+  if (om != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, true, false>(g, tA, tB, nullptr, dev, dev_err, s, *om);
   static OutMaps none{};
-  return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false>(g, tA, tB, ws, dev, dev_err, s, none);
+  if (ws != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, true>(g, tA, tB, ws, dev, dev_err, s, none);
+  return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, false>(g, tA, tB, nullptr, dev, dev_err, s, none);
 }
 
 }  // namespace

@@ -45,6 +45,12 @@ struct Gemm {
   int a_bcast;  // batch > 1 and stride_a == 0: every batch entry uses the same A
   int bias_m;   // bias has M entries (one per row) instead of N (one per column)
   PeerOut peers;  // also write C to these (same layout), n = 0: none
+  // Column-progress flags (CTA-pair kernel only; nullptr = none): after the
+  // output tile in pair-tile column tn is stored, each of the pair's CTAs
+  // adds 1 to col_flags[tn / flag_tiles] (system-scope release), so another
+  // stream can start on finished column groups while the GEMM runs.
+  int* col_flags = nullptr;
+  int flag_tiles = 0;
 };
 
 inline int elem_bytes(int dtype) { return dtype == CMPX_F32 ? 4 : 2; }
@@ -116,6 +122,11 @@ cudaError_t launch_fill_bias(const Gemm& g, cudaStream_t s);
 // computed in fp32 and rounded once).
 cudaError_t launch_add_bias(int dtype, void* C, const void* bias, int64_t rows, int64_t cols, cudaStream_t s);
 
+// cmpx_gemm for the CTA-pair kernel with column-progress flags (see
+// Gemm::col_flags); CMPX_ERR_UNSUPPORTED for anything that would not run the
+// 256-column pair-tile kernel on whole tiles.
+int run_gemm_flagged(const cmpx_gemm_args* args, int* flags, int flag_tiles, cudaStream_t s);
+
 // Device error word (see ptx.cuh DeviceError).
 int* device_error_word();
 
@@ -128,6 +139,9 @@ int encode_tmap_3d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, 
 
 // Programmatic dependent launch for the GEMM kernels (on unless CMPX_PDL=0).
 bool pdl_enabled();
+// Sleep between polls of a tile kernel's epilogue while it waits for the
+// next accumulator (CMPX_EPI_SLEEP_NS, default 0 = spin).
+unsigned epilogue_sleep_ns();
 // Fills `attr` (one slot) and cfg.attrs / cfg.numAttrs for a PDL launch, or
 // leaves cfg without attributes when PDL is off.
 inline void apply_pdl(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int used) {

@@ -86,6 +86,24 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   return mbar_wait_limit(bar, parity, abort, CMPX_WAIT_TIMEOUT_NS);
 }
+// The same bounded wait for long waits (an epilogue waiting for a whole
+// tile's main loop): after the first 64 polls each further poll is preceded
+// by a __nanosleep of sleep_ns, so the waiting warps stop competing for issue
+// slots and power with the MMA and TMA warps.  sleep_ns = 0: plain polling.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                uint32_t sleep_ns) {
+  if (sleep_ns == 0) return mbar_wait_limit(bar, parity, abort, CMPX_WAIT_TIMEOUT_NS);
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i >= 64) __nanosleep(sleep_ns);
+    if ((i & 15u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > CMPX_WAIT_TIMEOUT_NS) return false;
+    }
+  }
+}
 
 // ------------------------------------------------- programmatic dependent launch
 // A kernel launched with programmatic stream serialization may start while

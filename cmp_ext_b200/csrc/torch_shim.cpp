@@ -338,6 +338,46 @@ void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vecto
   check_status(cmpx_gemm(&args, current_stream()), "matmul_into");
 }
 
+// a @ b into `out` (this rank's rows of a row-sharded C) with the rows
+// copied to peer_out[p] on copy_streams[p % n] as tile columns finish
+// (cmpx_gemm_gather_ce).  flags: int32 device tensor of n_groups entries.
+void matmul_gather_ce(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vector<int64_t> peer_out,
+                      torch::Tensor flags, int64_t epoch, std::vector<int64_t> copy_streams) {
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "matmul_gather_ce: 2-D tensors expected");
+  TORCH_CHECK(a.is_cuda() && b.device() == a.device() && out.device() == a.device() && flags.device() == a.device(),
+              "matmul_gather_ce: one CUDA device");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type() && out.scalar_type() == a.scalar_type(), "Dtype mismatch");
+  TORCH_CHECK(a.size(1) == b.size(0), "Contracting dimension (K) mismatch");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == b.size(1) && out.stride(1) == 1,
+              "matmul_gather_ce: output shape mismatch");
+  TORCH_CHECK(flags.scalar_type() == at::kInt && flags.is_contiguous(), "matmul_gather_ce: int32 flags expected");
+  TORCH_CHECK(peer_out.size() <= 7 && copy_streams.size() >= (peer_out.empty() ? 0u : 1u),
+              "matmul_gather_ce: at most 7 peers and at least one copy stream");
+  const int dt = dtype_code(a.scalar_type());
+  TORCH_CHECK(dt == CMPX_F16 || dt == CMPX_BF16, "matmul_gather_ce: fp16 / bf16 only");
+  c10::cuda::CUDAGuard guard(a.device());
+  a = a.contiguous();
+  b = b.contiguous();
+  cmpx_gemm_args args = base_args(dt);
+  args.A = a.data_ptr();
+  args.B = b.data_ptr();
+  args.C = out.data_ptr();
+  args.M = a.size(0);
+  args.N = b.size(1);
+  args.K = a.size(1);
+  args.lda = args.K;
+  args.ldb = args.N;
+  args.ldc = out.stride(0);
+  args.b_layout = CMPX_B_KN;
+  std::vector<void*> peers(peer_out.size());
+  for (size_t i = 0; i < peer_out.size(); ++i) peers[i] = reinterpret_cast<void*>(peer_out[i]);
+  std::vector<cmpx_stream_t> cs(copy_streams.size());
+  for (size_t i = 0; i < copy_streams.size(); ++i) cs[i] = reinterpret_cast<cmpx_stream_t>(copy_streams[i]);
+  check_status(cmpx_gemm_gather_ce(&args, peers.data(), int(peers.size()), flags.data_ptr<int>(), int(flags.numel()),
+                                   static_cast<unsigned int>(epoch), current_stream(), cs.data(), int(cs.size())),
+               "matmul_gather_ce");
+}
+
 torch::Tensor fp16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kHalf, "fp16_matmul"); }
 torch::Tensor bf16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kBFloat16, "bf16_matmul"); }
 torch::Tensor fp32_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kFloat, "fp32_matmul"); }
@@ -356,6 +396,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp32_matmul", &fp32_matmul, "a[M,K] @ b[K,N] in fp32 (3xTF32)", py::arg("a"), py::arg("b"));
   m.def("_matmul_into", &matmul_into, "a @ b written into out (and peer copies of it) (internal)", py::arg("a"),
         py::arg("b"), py::arg("out"), py::arg("peer_out") = std::vector<int64_t>{});
+  m.def("_matmul_gather_ce", &matmul_gather_ce,
+        "a @ b into out with the rows copied to peer outputs on copy streams as tile columns finish (internal)",
+        py::arg("a"), py::arg("b"), py::arg("out"), py::arg("peer_out"), py::arg("flags"), py::arg("epoch"),
+        py::arg("copy_streams"));
   m.def("_set_path", &set_path, "force a kernel path for testing: auto, tc, skinny, simt");
   m.def("_matmul_path", &matmul_path, "kernel path cmpx_gemm picks for a packed (M,K)x(K,N) matmul");
   m.def("_version", []() { return std::string(cmpx_version()); });

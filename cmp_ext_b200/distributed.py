@@ -18,6 +18,8 @@ import torch.distributed as dist
 
 # Symmetric-memory outputs registered by gather_output(): data_ptr -> handle.
 _SYMM = {}
+# transport="ce" state per output: column-progress flags, call count, copy streams.
+_CE = {}
 
 
 def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
@@ -52,7 +54,7 @@ def default_op(dtype: torch.dtype) -> Callable[[torch.Tensor, torch.Tensor], tor
 
 def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = None, gather: bool = False,
                    chunks: int = 1, group=None, op=None, out: torch.Tensor | None = None,
-                   transport: str = "nccl") -> torch.Tensor:
+                   transport: str = "nccl", ce_groups: int = 4) -> torch.Tensor:
     """This rank's rows of A @ B, or (gather=True) the full product on every rank.
 
     a_shard: this rank's rows of A, as given by ``shard_rows(M, world, rank)``.
@@ -66,11 +68,16 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
        multiplied.
     op: the per-shard GEMM (defaults to cmp_ext_b200's *_matmul for the dtype;
        tests on CPU pass torch.matmul).
-    transport: "nccl" (all-gather after the GEMM) or "nvlink": the GEMM's
+    transport: "nccl" (all-gather after the GEMM), "nvlink" (the GEMM's
        epilogue stores every output tile to its own rows and, over NVLink, to
        the same rows of every peer's output, overlapping the exchange with the
-       remaining tiles; one device-side barrier then completes the gather.
-       Needs `out` from gather_output() and evenly divided rows.
+       remaining tiles) or "ce" (the GEMM counts finished tile columns in
+       device flags; one copy stream per peer waits on each group of columns
+       and copies it to the peer's output with the copy engines, so the
+       exchange overlaps the GEMM without taking SM time).  "nvlink" and
+       "ce" need `out` from gather_output() and evenly divided rows; a
+       device-side barrier before and after the call orders the reuse of
+       every rank's output.
     """
     op_is_default = op is None
     op = op or default_op(a_shard.dtype)
@@ -112,6 +119,28 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
         h.barrier(channel=0)  # every rank is done with the previous contents of its output
         cx._matmul_into(a_shard, b, out[rank * S:(rank + 1) * S], peers)
         h.barrier(channel=0)  # every rank's stores into every output are done
+        return out
+    elif transport == "ce":
+        h = _SYMM.get(out.data_ptr())
+        if h is None or out.shape != (M, N) or not out.is_contiguous():
+            raise ValueError("transport='ce' needs the output from gather_output(M, N, ...)")
+        if not op_is_default:
+            raise ValueError("transport='ce' runs the library's own GEMM (op must be None)")
+        import cmp_ext_b200 as cx
+
+        st = _CE.get(out.data_ptr())
+        if st is None:
+            st = {"flags": torch.zeros(ce_groups, dtype=torch.int32, device=out.device), "epoch": 0,
+                  "streams": [torch.cuda.Stream(out.device) for _ in range(max(1, world - 1))]}
+            _CE[out.data_ptr()] = st
+        st["epoch"] += 1
+        row_bytes = N * out.element_size()
+        offset = rank * S * row_bytes
+        peers = [int(h.buffer_ptrs[p]) + offset for p in range(world) if p != rank]
+        h.barrier(channel=0)  # every rank is done with the previous contents of its output
+        cx._matmul_gather_ce(a_shard, b, out[rank * S:(rank + 1) * S], peers, st["flags"], st["epoch"],
+                             [s.cuda_stream for s in st["streams"]])
+        h.barrier(channel=0)  # every rank's copies into every output have landed
         return out
     elif transport != "nccl":
         raise ValueError(f"unknown transport {transport!r}")

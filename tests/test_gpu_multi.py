@@ -48,6 +48,15 @@ for rep in range(2):
     assert not torch.isnan(C.float()).any(), "nvlink gather left rows unwritten"
     err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
     assert err <= 2 ** -7, ("nvlink", err)
+out2 = gather_output(M, N, torch.bfloat16, "cuda")
+for rep in range(3):  # copy-engine transport: flags are never reset, so repeat calls matter
+    out2.fill_(float("nan"))
+    dist.barrier()
+    C = sharded_matmul(A[r0:r1].contiguous(), B, M=M, gather=True, transport="ce", out=out2)
+    torch.cuda.synchronize()
+    assert not torch.isnan(C.float()).any(), "ce gather left rows unwritten"
+    err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
+    assert err <= 2 ** -7, ("ce", err)
 from cmp_ext_b200.distributed import sharded_host_matmul
 hA = A[r0:r1].cpu().pin_memory()
 hB = B.cpu().pin_memory()

@@ -499,6 +499,51 @@ def sub_workload(cid, timer, P, args, device, world, rank, path=None, steps=None
         torch.cuda.empty_cache()
 
 
+def attention_record(timer, P, args, device, dtype=torch.float16):
+    """cmpext3.attention on the reference's own benchmark shape
+    (tools/bench.py:276-287: B=8, H=8, L=1024, D=128, scale 1/sqrt(D)),
+    4 rotating input sets (402 MB > 3 x L2): FLOPs 4*B*H*L^2*D (QK^T and PV)."""
+    import cmp_ext_b200 as cx
+
+    B, H, L, D = 8, 8, 1024, 128
+    g = torch.Generator(device=device).manual_seed(0)
+    sets = [tuple(torch.randn(B, H, L, D, generator=g, device=device).to(dtype) for _ in range(3)) for _ in range(4)]
+    st = {"i": 0}
+    scale = 1.0 / D ** 0.5
+
+    def step():
+        q, k, v = sets[st["i"] % len(sets)]
+        st["i"] += 1
+        st["out"], st["qkv"] = cx.attention(q, k, v, scale=scale), (q, k, v)
+
+    K = max(3, min(args.steps, 20))
+    ms, clocks = timer.run(step, K, 3)
+    launch_ms = timer.isolated(step, 5)
+    q, k, v = st["qkv"]
+    # fp64 check of 64 query rows of one (batch, head)
+    idx = torch.linspace(0, L - 1, 64, device=device).long()
+    s64 = (q[1, 3, idx].double() @ k[1, 3].double().t()) * scale
+    want = torch.softmax(s64, dim=-1) @ v[1, 3].double()
+    err = float((st["out"][1, 3, idx].double() - want).abs().max() / want.abs().max())
+    fl = 4.0 * B * H * L * L * D
+    ach = fl / (ms / K / 1e3) / 1e12
+    peak, kind = pick_peak(P, clocks)
+    rec = {"workload": f"attention {B}x{H}x{L}x{D} {KIND_NAMES[dtype]} (reference tools/bench.py shape)",
+           "kernel": "attention_tc_kernel", "value": ach, "unit": "TFLOP/s", "ms_per_step": ms / K, "steps": K,
+           "clocks": clocks, "err_vs_fp64_rows": err, "l2": "4 resident input sets rotated per step",
+           "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "peak_kind": kind, "frac": ach / peak,
+                        "unit": "TFLOP/s", "flops_per_step": fl},
+           "isolated_launch": {"ms": launch_ms, "achieved": fl / (launch_ms / 1e3) / 1e12,
+                               "frac": fl / (launch_ms / 1e3) / 1e12 / P["bf16_tflops"]}}
+    sets.clear()
+    st.clear()
+    torch.cuda.empty_cache()
+    return rec
+
+
+KIND_NAMES = {torch.float16: "fp16", torch.bfloat16: "bf16", torch.float32: "fp32"}
+
+
 def gathered_record(cfg, transport, timer, P, args, device, world, rank):
     """Config 3 M-sharded with the all-gather of C (every rank ends with the
     whole C), and a check of the gathered C: sampled rows of every rank's
@@ -636,6 +681,11 @@ def run_ours(args):
                 sub[f"config{cid}"] = sub_workload(cid, timer, P, args, device, world, rank)
             sub["config5_tf32x3"] = sub_workload(5, timer, P, args, device, world, rank, path="tc")
             sub["config5_simt"] = sub_workload(5, timer, P, args, device, world, rank, path="simt", steps=3)
+            for dt in (torch.float16, torch.bfloat16):
+                try:
+                    sub[f"attention_{KIND_NAMES[dt]}"] = attention_record(timer, P, args, device, dt)
+                except Exception as ex:  # reported, never hidden
+                    sub[f"attention_{KIND_NAMES[dt]}"] = {"error": repr(ex)[:300]}
         else:
             c3 = CONFIGS[3]
             if c3.M % world == 0:

@@ -8,6 +8,8 @@ reference's pybind module, src/main.cpp:1594-1602, plus the 2-D forms):
     conv2d(input, weight, bias=None, stride=1, padding=0, dilation=1, groups=1)
                                        the 1x1 / stride 1 / padding 0 case, as one
                                        batched GEMM on NCHW (no layout copies)
+    attention(query, key, value, scale=None)
+                                       softmax(scale * Q K^T) V on [B, H, S, D]
     fp16_matmul(a, b) / bf16_matmul(a, b) / fp32_matmul(a, b)
                                        a[M,K] @ b[K,N] -> [M,N]
 
@@ -24,7 +26,7 @@ import torch  # noqa: F401  (loads libtorch / c10 before the shim)
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcmpx.so")
 
-_OPS = ("linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul", "_set_path", "_matmul_into", "_matmul_gather_ce", "version")
+_OPS = ("linear", "bmm", "conv2d", "attention", "fp16_matmul", "bf16_matmul", "fp32_matmul", "_set_path", "_matmul_into", "_matmul_gather_ce", "version")
 
 
 def _load_ext():
@@ -50,4 +52,4 @@ def __getattr__(name):
     raise AttributeError(f"module 'cmp_ext_b200' has no attribute {name!r}")
 
 
-__all__ = ["linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul", "LIB_PATH", "version"]
+__all__ = ["linear", "bmm", "conv2d", "attention", "fp16_matmul", "bf16_matmul", "fp32_matmul", "LIB_PATH", "version"]

@@ -27,7 +27,8 @@ INCLUDE = os.path.join(REPO, "include")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["cmpx_api.cu", "gemm_tc.cu", "gemm_tc2.cu", "gemm_skinny.cu", "gemm_simt.cu", "cmpx_selftest.cu", "gather_ce.cu"]
+CU_SOURCES = ["cmpx_api.cu", "gemm_tc.cu", "gemm_tc2.cu", "gemm_skinny.cu", "gemm_simt.cu", "cmpx_selftest.cu", "gather_ce.cu",
+              "attention.cu"]
 HEADERS = ["ptx.cuh", "internal.h"]
 LIB = os.path.join(HERE, "libcmpx.so")
 SHIM_SRC = os.path.join(CSRC, "torch_shim.cpp")

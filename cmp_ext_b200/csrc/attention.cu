@@ -1,0 +1,573 @@
+// Scaled dot-product attention O = softmax(scale * Q K^T) V for [B, H, S, D]
+// tensors, replacing the reference's attention kernels
+// (src/cuda/fp16_attention.cu:77 flash_attention_fp16_optimized,
+//  src/cuda/bf16_attention.cu:43 attention_bf16_kernel,
+//  src/cuda/fp32_attention.cu:35 attention_fp32_strict_kernel;
+//  launchers declared at src/main.cpp:48-50, wrapper src/main.cpp:1027-1098).
+//
+// fp16 / bf16 with D = 64 or 128: a tcgen05 flash-attention kernel.  One CTA
+// owns 128 query rows of one (batch, head):
+//   * warp 0 (TMA): Q once, then K_j and V_j blocks of 128 keys into two
+//     separate double-buffered rings (a K slot frees after its QK^T MMA, a V
+//     slot after its PV MMA, so the next K block streams in early);
+//   * warp 1 (one thread): S_j = Q K_j^T into one of two 128-column TMEM
+//     buffers (M 128, N 128, K = D, both operands K-major), then
+//     O_j = P_j V_j into one of two D-column TMEM buffers (A = P from shared
+//     memory, B = V_j N-major), ordered QK_0, QK_1, PV_0, QK_2, PV_1, ... so
+//     one score block is computed while the previous one is in softmax;
+//   * warps 2-9 (two threads per query row, each owning half of the keys
+//     of a block and half of the output columns): read S_j from TMEM, keep
+//     the running row maximum m (both threads of a row read the whole row,
+//     so they agree on it without exchanging anything) and a partial sum l
+//     in fp32 (base-2 exponent with scale * log2 e folded in), write their
+//     half of P_j = exp2(s - m) as 16-bit values into shared memory in the
+//     128-byte-swizzled K-major layout the MMA reads, then fold their half
+//     of the previous block's O_{j-1} into fp32 registers:
+//     O = O * exp2(m_{j-2} - m_{j-1}) + O_{j-1}.  Finally the two partial
+//     sums are combined through shared memory and O / l is rounded once to
+//     the output type.
+// Every product accumulates in fp32; the reference accumulates fp16 in
+// fp16 (src/cuda/fp16_attention.cu:128-239) and normalises with an fp16
+// reciprocal, so this kernel's error is an order of magnitude lower.
+//
+// Other shapes and fp32: a CUDA-core kernel (one warp per query row, the
+// same online softmax in fp32, fp32 accumulation).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdio>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace cmpx {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct AttnCfg {
+  static constexpr int QCH = D / 64;                 // 64-element (128-byte) chunks of D
+  static constexpr int TILE_BYTES = 128 * D * 2;     // 128 rows x D x 2 B
+  static constexpr int P_BYTES = 128 * 128 * 2;      // P block: 128 rows x 128 keys x 2 B
+  static constexpr int KST = 2, VST = 2;             // ring depths
+  static constexpr size_t SMEM = size_t(TILE_BYTES) * (1 + KST + VST) + 2 * P_BYTES + 1024 + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;         // S0 S1 (128 each) then O0 O1 (D each)
+  static_assert(D == 64 || D == 128, "tensor-core attention supports D = 64 or 128");
+};
+
+struct AttnParams {
+  void* O;
+  int S, qtiles;
+  float scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ void rec_err(int* err, volatile int* abort, int code) {
+  *abort = 1;
+  atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int FMT, int D>
+__global__ void __launch_bounds__(320, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using Cfg = AttnCfg<D>;
+  using T = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
+  constexpr uint32_t IDESC_QK = make_idesc(uint32_t(FMT), 0u, 0u, 128, 128);
+  constexpr uint32_t IDESC_PV = make_idesc(uint32_t(FMT), 0u, 1u, 128, D);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + Cfg::TILE_BYTES;                   // [KST]
+  uint8_t* sV = sK + Cfg::KST * Cfg::TILE_BYTES;        // [VST]
+  uint8_t* sP = sV + Cfg::VST * Cfg::TILE_BYTES;        // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + Cfg::KST;
+  uint64_t* v_full = k_empty + Cfg::KST;
+  uint64_t* v_empty = v_full + Cfg::VST;
+  uint64_t* s_full = v_empty + Cfg::VST;   // [2]
+  uint64_t* s_empty = s_full + 2;          // [2]
+  uint64_t* p_full = s_empty + 2;          // [2]
+  uint64_t* o_full = p_full + 2;           // [2]
+  uint64_t* o_empty = o_full + 2;          // [2]
+  uint64_t* drain = o_empty + 2;
+  uint64_t* l_bar = drain + 1;             // the 256 partial row sums are in l_part
+  float* l_part = reinterpret_cast<float*>(l_bar + 1);  // [2][128]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(l_part + 256);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x / p.qtiles;
+  const int q0 = (blockIdx.x - bh * p.qtiles) * 128;
+  const int nkv = (p.S + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < Cfg::KST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < Cfg::VST; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 256);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 256);
+    }
+    mbar_init(drain, 1);
+    mbar_init(l_bar, 256);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, Cfg::TILE_BYTES);
+#pragma unroll
+      for (int c = 0; c < Cfg::QCH; ++c) tma_load_3d(sQ + c * 16384, &tmQ, q_full, c * 64, q0, bh);
+      bool ok = true;
+      int kissued = 0, vissued = 0;
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int ks = j % Cfg::KST, vs = j % Cfg::VST;
+        if (!mbar_wait(&k_empty[ks], ((j / Cfg::KST) & 1) ^ 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutEmpty);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[ks], Cfg::TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < Cfg::QCH; ++c)
+          tma_load_3d(sK + ks * Cfg::TILE_BYTES + c * 16384, &tmK, &k_full[ks], c * 64, j * 128, bh);
+        ++kissued;
+        if (!mbar_wait(&v_empty[vs], ((j / Cfg::VST) & 1) ^ 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutEmpty);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[vs], Cfg::TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < Cfg::QCH; ++c)
+          tma_load_3d(sV + vs * Cfg::TILE_BYTES + c * 16384, &tmV, &v_full[vs], c * 64, j * 128, bh);
+        ++vissued;
+      }
+      if (!ok) {
+        // let the copies in flight land before the CTA exits (bounded waits)
+        volatile int never = 0;
+        mbar_wait(q_full, 0, &never);
+        for (int j = (kissued > Cfg::KST ? kissued - Cfg::KST : 0); j < kissued; ++j)
+          mbar_wait(&k_full[j % Cfg::KST], (j / Cfg::KST) & 1, &never);
+        for (int j = (vissued > Cfg::VST ? vissued - Cfg::VST : 0); j < vissued; ++j)
+          mbar_wait(&v_full[j % Cfg::VST], (j / Cfg::VST) & 1, &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      if (!ok) rec_err(p.err, abort_flag, kDevTimeoutFull);
+      const uint32_t q_addr = smem_u32(sQ);
+      auto issue_qk = [&](int j) -> bool {
+        const int ks = j % Cfg::KST, b = j & 1;
+        if (!mbar_wait(&k_full[ks], (j / Cfg::KST) & 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutFull);
+          return false;
+        }
+        if (!mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutAccEmpty);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + ks * Cfg::TILE_BYTES);
+        const uint32_t d_tmem = tmem_base + uint32_t(b * 128);
+#pragma unroll
+        for (int c = 0; c < Cfg::QCH; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(d_tmem, make_sdesc_sw128(q_addr + c * 16384 + kk * 32, 16, 1024),
+                    make_sdesc_sw128(k_addr + c * 16384 + kk * 32, 16, 1024), IDESC_QK, (c | kk) != 0 ? 1u : 0u);
+        mma_commit(&s_full[b]);
+        mma_commit(&k_empty[ks]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int vs = j % Cfg::VST, b = j & 1;
+        if (!mbar_wait(&p_full[b], (j >> 1) & 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutFull);
+          return false;
+        }
+        if (!mbar_wait(&v_full[vs], (j / Cfg::VST) & 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutFull);
+          return false;
+        }
+        if (!mbar_wait(&o_empty[b], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutAccEmpty);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + b * Cfg::P_BYTES);
+        const uint32_t v_addr = smem_u32(sV + vs * Cfg::TILE_BYTES);
+        const uint32_t d_tmem = tmem_base + 256u + uint32_t(b * D);
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(d_tmem, make_sdesc_sw128(p_addr + c2 * 16384 + kk * 32, 16, 1024),
+                    make_sdesc_sw128(v_addr + (c2 * 64 + kk * 16) * 128, 16384, 1024), IDESC_PV,
+                    (c2 | kk) != 0 ? 1u : 0u);
+        mma_commit(&o_full[b]);
+        mma_commit(&v_empty[vs]);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      if (ok && nkv > 1) ok = issue_qk(1);
+      for (int j = 0; ok && j < nkv; ++j) {
+        ok = issue_pv(j);
+        if (ok && j + 2 < nkv) ok = issue_qk(j + 2);
+      }
+      if (!ok) {
+        mma_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + output (warps 2..9)
+    constexpr int DH = D / 2;        // output columns per thread
+    const int qw = warp & 3;         // TMEM lane quarter this warp may access
+    const int h = (warp - 2) >> 2;   // which half of the keys / output columns
+    const int r = qw * 32 + lane;    // row of this CTA's 128
+    const uint32_t t_lane = tmem_base + (uint32_t(qw * 32) << 16);
+    float o[DH];
+#pragma unroll
+    for (int i = 0; i < DH; ++i) o[i] = 0.0f;
+    float m_run = -INFINITY, l = 0.0f;
+    float m_prev = -INFINITY;  // running max of the block whose O was folded last
+    float m_hist = -INFINITY;  // running max of the block still to fold
+    bool ok = true;
+    // Iteration j: softmax of block j (j < nkv), then fold O_{j-1} (j >= 1).
+    // One fold site keeps the register accumulator in registers.
+#pragma unroll 1
+    for (int j = 0; j <= nkv; ++j) {
+      float m_new = m_run;
+      if (j < nkv) {
+        const int b = j & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t s_addr = t_lane + uint32_t(b * 128);
+        const int kv0 = j * 128;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t x[16];
+          tmem_ld_32x32b_x16(s_addr + c * 16, x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (kv0 + c * 16 + i < p.S) mx = fmaxf(mx, __uint_as_float(x[i]) * p.scale_log2);
+        }
+        m_new = fmaxf(m_run, mx);
+        float sum = 0.0f;
+        // this thread's keys [64h, 64h + 64) are chunk h of P's two 64-key chunks
+        uint8_t* prow = sP + b * Cfg::P_BYTES + h * 16384 + r * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t x[16];
+          const int k0 = h * 64 + c * 16;
+          tmem_ld_32x32b_x16(s_addr + k0, x);
+          tmem_ld_wait();
+          float pv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            pv[i] = (kv0 + k0 + i < p.S) ? exp2f(fmaf(__uint_as_float(x[i]), p.scale_log2, -m_new)) : 0.0f;
+            sum += pv[i];
+          }
+          // keys [k0, k0 + 16): 16-byte units 2c and 2c + 1 of the row's 128 bytes
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            uint4 q;
+            q.x = pack2(pv[g * 8 + 0], pv[g * 8 + 1], (T*)nullptr);
+            q.y = pack2(pv[g * 8 + 2], pv[g * 8 + 3], (T*)nullptr);
+            q.z = pack2(pv[g * 8 + 4], pv[g * 8 + 5], (T*)nullptr);
+            q.w = pack2(pv[g * 8 + 6], pv[g * 8 + 7], (T*)nullptr);
+            const int u = c * 2 + g;
+            *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = q;
+          }
+        }
+        l = l * exp2f(m_run - m_new) + sum;
+        m_run = m_new;
+        tc_fence_before();
+        mbar_arrive(&s_empty[b]);   // S buffer may be overwritten by QK_{j+2}
+        fence_proxy_async_smem();   // P visible to the tensor core
+        mbar_arrive(&p_full[b]);
+      }
+      if (j >= 1) {
+        const int b = (j - 1) & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_full[b], ((j - 1) >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float beta = exp2f(m_prev - m_hist);  // 0 while nothing has been folded
+#pragma unroll
+        for (int c = 0; c < DH / 16; ++c) {
+          uint32_t x[16];
+          tmem_ld_32x32b_x16(t_lane + 256u + uint32_t(b * D + h * DH + c * 16), x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[c * 16 + i] = fmaf(o[c * 16 + i], beta, __uint_as_float(x[i]));
+        }
+        tc_fence_before();
+        mbar_arrive(&o_empty[b]);
+        m_prev = m_hist;
+      }
+      m_hist = m_new;
+    }
+    if (ok) {
+      // combine the two partial row sums (bounded wait: a thread that gave
+      // up never arrives, and its partner then gives up too)
+      l_part[h * 128 + r] = l;
+      mbar_arrive(l_bar);
+      ok = __all_sync(0xffffffffu, mbar_wait(l_bar, 0, abort_flag));
+    }
+    if (!ok) {
+      if (lane == 0) rec_err(p.err, abort_flag, kDevTimeoutAccFull);
+    } else if (q0 + r < p.S) {
+      const float inv = 1.0f / (l_part[r] + l_part[128 + r]);
+      T* orow = reinterpret_cast<T*>(p.O) + (size_t(bh) * p.S + q0 + r) * D + h * DH;
+#pragma unroll
+      for (int g = 0; g < DH / 8; ++g) {
+        uint4 q;
+        q.x = pack2(o[g * 8 + 0] * inv, o[g * 8 + 1] * inv, (T*)nullptr);
+        q.y = pack2(o[g * 8 + 2] * inv, o[g * 8 + 3] * inv, (T*)nullptr);
+        q.z = pack2(o[g * 8 + 4] * inv, o[g * 8 + 5] * inv, (T*)nullptr);
+        q.w = pack2(o[g * 8 + 6] * inv, o[g * 8 + 7] * inv, (T*)nullptr);
+        reinterpret_cast<uint4*>(orow)[g] = q;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ CUDA cores
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p);
+template <>
+__device__ __forceinline__ float ldf<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ldf<__half>(const __half* p) { return __half2float(*p); }
+template <>
+__device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void stf(float* p, float v) { *p = v; }
+__device__ __forceinline__ void stf(__half* p, float v) { *p = __float2half_rn(v); }
+__device__ __forceinline__ void stf(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// One warp per query row; lane d holds output columns d, d+32, ... (up to
+// kSimtMaxD / 32 of them).  Online softmax in fp32 over all S keys.
+constexpr int kSimtMaxD = 512;
+
+template <typename T>
+__global__ void __launch_bounds__(128) attention_simt_kernel(const T* __restrict__ Q, const T* __restrict__ K,
+                                                             const T* __restrict__ V, T* __restrict__ O,
+                                                             long long rows, int S, int D, float scale_log2) {
+  const long long row = blockIdx.x * 4LL + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const long long bh = row / S;
+  const T* q = Q + row * D;
+  const T* kb = K + bh * S * (long long)D;
+  const T* vb = V + bh * S * (long long)D;
+  constexpr int NV = kSimtMaxD / 32;
+  float qv[NV], acc[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int d = lane + 32 * i;
+    qv[i] = d < D ? ldf(q + d) : 0.0f;
+    acc[i] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  for (int k = 0; k < S; ++k) {
+    const T* kr = kb + (long long)k * D;
+    float dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) dot = fmaf(qv[i], ldf(kr + d), dot);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float s = dot * scale_log2;
+    const float m_new = fmaxf(m, s);
+    const float alpha = exp2f(m - m_new);
+    const float pk = exp2f(s - m_new);
+    l = l * alpha + pk;
+    const T* vr = vb + (long long)k * D;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) acc[i] = fmaf(acc[i], alpha, pk * ldf(vr + d));
+    }
+    m = m_new;
+  }
+  const float inv = 1.0f / l;
+  T* orow = O + row * D;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int d = lane + 32 * i;
+    if (d < D) stf(orow + d, acc[i] * inv);
+  }
+}
+
+template <int FMT, int D>
+cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int64_t BH, int64_t S, float scale,
+                      int* err, cudaStream_t s) {
+  using Cfg = AttnCfg<D>;
+  auto kern = attention_tc_kernel<FMT, D>;
+  static_assert(Cfg::SMEM <= 232448, "shared memory budget");
+  static unsigned long long smem_set = 0;
+  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
+  if (e != cudaSuccess) return e;
+  const int dt = FMT == 0 ? CMPX_F16 : CMPX_BF16;
+  CUtensorMap tq, tk, tv;
+  if (encode_tmap_3d(&tq, dt, Q, D, S, BH, D, S * D, 64, 128) != CMPX_OK ||
+      encode_tmap_3d(&tk, dt, K, D, S, BH, D, S * D, 64, 128) != CMPX_OK ||
+      encode_tmap_3d(&tv, dt, V, D, S, BH, D, S * D, 64, 128) != CMPX_OK)
+    return cudaErrorInvalidValue;
+  AttnParams p;
+  p.O = O;
+  p.S = int(S);
+  p.qtiles = int((S + 127) / 128);
+  p.scale_log2 = scale * kLog2e;
+  p.err = err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(BH * p.qtiles));
+  cfg.blockDim = dim3(320);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  apply_pdl(cfg, attr, 0);
+  return cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p);
+}
+
+template <typename T>
+cudaError_t launch_simt_attn(const void* Q, const void* K, const void* V, void* O, int64_t BH, int64_t S, int64_t D,
+                             float scale, cudaStream_t s) {
+  const long long rows = BH * S;
+  const long long blocks = (rows + 3) / 4;
+  attention_simt_kernel<T><<<unsigned(blocks), 128, 0, s>>>(static_cast<const T*>(Q), static_cast<const T*>(K),
+                                                            static_cast<const T*>(V), static_cast<T*>(O), rows,
+                                                            int(S), int(D), scale * kLog2e);
+  return cudaGetLastError();
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int attention_path(int dtype, const void* Q, const void* K, const void* V, const void* O, int64_t D, int requested) {
+  const bool tc_ok = (dtype == CMPX_F16 || dtype == CMPX_BF16) && (D == 64 || D == 128) && al16(Q) && al16(K) &&
+                     al16(V) && al16(O);
+  if (requested == CMPX_PATH_TC) return tc_ok ? CMPX_PATH_TC : -1;
+  if (requested == CMPX_PATH_SIMT) return D <= kSimtMaxD ? CMPX_PATH_SIMT : -1;
+  if (requested != CMPX_PATH_AUTO) return -1;
+  if (tc_ok) return CMPX_PATH_TC;
+  return D <= kSimtMaxD ? CMPX_PATH_SIMT : -1;
+}
+
+}  // namespace cmpx
+
+using namespace cmpx;
+
+extern "C" int cmpx_attention(int dtype, const void* Q, const void* K, const void* V, void* O, int64_t B, int64_t H,
+                              int64_t S, int64_t D, float scale, int path, cmpx_stream_t stream) {
+  if (dtype != CMPX_F16 && dtype != CMPX_BF16 && dtype != CMPX_F32) return CMPX_ERR_INVALID_ARG;
+  if (B < 0 || H < 0 || S < 0 || D < 0) return CMPX_ERR_INVALID_ARG;
+  if (B == 0 || H == 0 || S == 0 || D == 0) return CMPX_OK;
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) return CMPX_ERR_INVALID_ARG;
+  if (S > (int64_t(1) << 31) - 1 || B * H > (int64_t(1) << 31) - 1) return CMPX_ERR_UNSUPPORTED;
+  const int pth = attention_path(dtype, Q, K, V, O, D, path);
+  if (pth < 0) return CMPX_ERR_UNSUPPORTED;
+  DeviceInfo dev;
+  int* err = nullptr;
+  int st = device_facts(&dev, &err);
+  if (st != CMPX_OK) return st;
+  const int64_t BH = B * H;
+  cudaError_t e;
+  if (pth == CMPX_PATH_TC) {
+    if (BH * ((S + 127) / 128) > 0x7fffffffLL) return CMPX_ERR_UNSUPPORTED;
+    if (dtype == CMPX_F16)
+      e = D == 64 ? launch_tc<0, 64>(Q, K, V, O, BH, S, scale, err, stream)
+                  : launch_tc<0, 128>(Q, K, V, O, BH, S, scale, err, stream);
+    else
+      e = D == 64 ? launch_tc<1, 64>(Q, K, V, O, BH, S, scale, err, stream)
+                  : launch_tc<1, 128>(Q, K, V, O, BH, S, scale, err, stream);
+  } else {
+    if ((BH * S + 3) / 4 > 0x7fffffffLL) return CMPX_ERR_UNSUPPORTED;
+    e = dtype == CMPX_F16    ? launch_simt_attn<__half>(Q, K, V, O, BH, S, D, scale, stream)
+        : dtype == CMPX_BF16 ? launch_simt_attn<__nv_bfloat16>(Q, K, V, O, BH, S, D, scale, stream)
+                             : launch_simt_attn<float>(Q, K, V, O, BH, S, D, scale, stream);
+  }
+  return e == cudaSuccess ? CMPX_OK : CMPX_ERR_CUDA;
+}
+
+extern "C" int cmpx_attention_select_path(int dtype, const void* Q, const void* K, const void* V, const void* O,
+                                          int64_t D, int path) {
+  if (dtype != CMPX_F16 && dtype != CMPX_BF16 && dtype != CMPX_F32) return -1;
+  return attention_path(dtype, Q, K, V, O, D, path);
+}
+
+// Reference-compatible C++-linkage launchers (src/main.cpp:48-50): legacy
+// default stream, no status; a failure is reported on stderr.
+static void report_attn(const char* what, int st) {
+  if (st != CMPX_OK) fprintf(stderr, "cmpx %s error: %s\n", what, cmpx_status_string(st));
+}
+CMPX_API void launch_attention_fp32(const float* q, const float* k, const float* v, float* output, int B, int H, int S,
+                                    int D, float scale) {
+  report_attn("launch_attention_fp32", cmpx_attention(CMPX_F32, q, k, v, output, B, H, S, D, scale, 0, nullptr));
+}
+CMPX_API void launch_attention_fp16(const void* q, const void* k, const void* v, void* output, int B, int H, int S,
+                                    int D, float scale) {
+  report_attn("launch_attention_fp16", cmpx_attention(CMPX_F16, q, k, v, output, B, H, S, D, scale, 0, nullptr));
+}
+CMPX_API void launch_attention_bf16(const void* q, const void* k, const void* v, void* output, int B, int H, int S,
+                                    int D, float scale) {
+  report_attn("launch_attention_bf16", cmpx_attention(CMPX_BF16, q, k, v, output, B, H, S, D, scale, 0, nullptr));
+}

@@ -20,6 +20,7 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/extension.h>
 
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -378,6 +379,40 @@ void matmul_gather_ce(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::
                "matmul_gather_ce");
 }
 
+// cmpext3.attention(query, key, value, scale=None) -- custom_attention_forward
+// (reference src/main.cpp:1027-1098): same checks, messages and order, same
+// default scale 1/sqrt(D) computed in fp32, fresh contiguous [B, H, S, D]
+// output.  Adds a dtype-equality check and rejects non-CUDA tensors; the
+// reference's "S <= 4096" warning does not apply (the kernel tiles S).
+torch::Tensor attention(torch::Tensor query, torch::Tensor key, torch::Tensor value,
+                        c10::optional<double> scale_arg) {
+  TORCH_CHECK(query.dim() == 4, "Query must be 4D (Batch, Head, Seq, Dim)");
+  TORCH_CHECK(key.dim() == 4, "Key must be 4D");
+  TORCH_CHECK(value.dim() == 4, "Value must be 4D");
+  const int64_t B = query.size(0), H = query.size(1), S = query.size(2), D = query.size(3);
+  TORCH_CHECK(key.size(0) == B && key.size(1) == H && key.size(2) == S && key.size(3) == D, "Key shape mismatch");
+  TORCH_CHECK(value.size(0) == B && value.size(1) == H && value.size(2) == S && value.size(3) == D,
+              "Value shape mismatch");
+  TORCH_CHECK(query.device() == key.device() && query.device() == value.device(), "Device mismatch");
+  TORCH_CHECK(query.is_cuda(), "attention expects CUDA tensors");
+  TORCH_CHECK(key.scalar_type() == query.scalar_type() && value.scalar_type() == query.scalar_type(),
+              "Dtype mismatch");
+  const int dt = dtype_code(query.scalar_type());
+  TORCH_CHECK(dt >= 0, "Unsupported dtype for attention");
+  c10::cuda::CUDAGuard guard(query.device());
+  query = query.contiguous();
+  key = key.contiguous();
+  value = value.contiguous();
+  torch::Tensor out = torch::empty({B, H, S, D}, query.options());
+  float scale = 1.0f / std::sqrt(static_cast<float>(D));
+  if (scale_arg.has_value()) scale = static_cast<float>(scale_arg.value());
+  const int path = g_forced_path == CMPX_PATH_SIMT ? CMPX_PATH_SIMT : CMPX_PATH_AUTO;
+  check_status(cmpx_attention(dt, query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), B, H, S, D,
+                              scale, path, current_stream()),
+               "attention");
+  return out;
+}
+
 torch::Tensor fp16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kHalf, "fp16_matmul"); }
 torch::Tensor bf16_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kBFloat16, "bf16_matmul"); }
 torch::Tensor fp32_matmul(torch::Tensor a, torch::Tensor b) { return matmul_2d(a, b, at::kFloat, "fp32_matmul"); }
@@ -396,6 +431,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp32_matmul", &fp32_matmul, "a[M,K] @ b[K,N] in fp32 (3xTF32)", py::arg("a"), py::arg("b"));
   m.def("_matmul_into", &matmul_into, "a @ b written into out (and peer copies of it) (internal)", py::arg("a"),
         py::arg("b"), py::arg("out"), py::arg("peer_out") = std::vector<int64_t>{});
+  m.def("attention", &attention, "scaled dot-product attention (cmpext3.attention)", py::arg("query"),
+        py::arg("key"), py::arg("value"), py::arg("scale") = py::none());
   m.def("_matmul_gather_ce", &matmul_gather_ce,
         "a @ b into out with the rows copied to peer outputs on copy streams as tile columns finish (internal)",
         py::arg("a"), py::arg("b"), py::arg("out"), py::arg("peer_out"), py::arg("flags"), py::arg("epoch"),

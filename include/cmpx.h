@@ -9,6 +9,7 @@
  *   void launch_matmul_fp32(const float* A, const float* B, float* C, int M, int N, int K);
  *   void launch_matmul_bf16(const void* A, const void* B, void* C, int M, int N, int K);
  *   void launch_add_bias_{fp16,fp32,bf16}(void* C, const void* bias, int rows, int cols);
+ *   void launch_attention_{fp32,fp16,bf16}(q, k, v, output, int B, int H, int S, int D, float scale);
  *
  *   (reference src/main.cpp:12-19; definitions src/cuda/fp16_matmul.cu:301-366,
  *    src/cuda/fp32_matmul.cu:236-287, src/cuda/bf16_matmul.cu:232-317)
@@ -191,6 +192,27 @@ CMPX_API int cmpx_add_bias(int dtype, void* C, const void* bias, int64_t rows, i
  * start of every call. */
 CMPX_API int cmpx_matmul_skinny_noalloc(int dtype, const void* A, const void* B, void* C, const void* bias,
                                         int64_t M, int64_t N, int64_t K, int b_layout, cmpx_stream_t stream);
+
+/* Scaled dot-product attention O = softmax(scale * Q K^T) V.  Replaces
+ * launch_attention_{fp32,fp16,bf16} (reference src/main.cpp:48-50;
+ * src/cuda/fp16_attention.cu:158-186, src/cuda/bf16_attention.cu:97-104,
+ * src/cuda/fp32_attention.cu:200-217), which libcmpx.so also exports under
+ * their C++ names (legacy default stream, no status).
+ *
+ * Q, K, V, O: contiguous [B, H, S, D] device tensors of `dtype` (the same S
+ * for queries and keys, as in the reference).  No mask.  fp16 / bf16 with
+ * D = 64 or 128 and 16-byte aligned pointers run a tcgen05 flash-attention
+ * kernel (QK^T and PV on the tensor cores, fp32 accumulation, online
+ * softmax in fp32); other D up to 512 and fp32 run a CUDA-core kernel with
+ * the same fp32 arithmetic.  path: CMPX_PATH_AUTO, CMPX_PATH_TC or
+ * CMPX_PATH_SIMT (CMPX_ERR_UNSUPPORTED when the forced path cannot run the
+ * shape). */
+CMPX_API int cmpx_attention(int dtype, const void* Q, const void* K, const void* V, void* O, int64_t B, int64_t H,
+                            int64_t S, int64_t D, float scale, int path, cmpx_stream_t stream);
+
+/* Which attention path cmpx_attention would take (cmpx_path value), or -1. */
+CMPX_API int cmpx_attention_select_path(int dtype, const void* Q, const void* K, const void* V, const void* O,
+                                        int64_t D, int path);
 
 /* Reads and clears the device-side error word of the current device
  * (synchronises the device).  *code receives the first error a kernel

@@ -119,6 +119,46 @@ def _load_ref():
     return _ref
 
 
+def ref_attention_supported(dtype: str, S: int, D: int) -> bool:
+    """Shapes the reference's attention kernels handle without reading out
+    of bounds (read from their sources): the fp16 flash kernel indexes D as
+    exactly 128 (src/cuda/fp16_attention.cu:133-160); the fp32 kernel keeps
+    D <= 128 registers and loads float4s (src/cuda/fp32_attention.cu:66-110);
+    the bf16 kernel keeps S fp32 logits in the default 48 KB of shared
+    memory (src/cuda/bf16_attention.cu:97-103)."""
+    if dtype == "f16":
+        return D == 128
+    if dtype == "f32":
+        return D % 4 == 0 and D <= 128
+    return S * 4 <= 48 * 1024
+
+
+def ref_gpu_attention(dtype: str, q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, B: int, H: int, S: int, D: int,
+                      scale: float) -> None:
+    """Runs the reference's own attention kernel on device pointers."""
+    if not ref_attention_supported(dtype, S, D):
+        raise ValueError(f"the reference's {dtype} attention kernel does not handle S={S}, D={D}")
+    lib = _load_ref()
+    lib.ref_attention.restype = ctypes.c_int
+    lib.ref_attention.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                  ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]
+    rc = lib.ref_attention(DTYPE_CODE[dtype], q_ptr, k_ptr, v_ptr, o_ptr, B, H, S, D, scale)
+    if rc != 0:
+        raise RuntimeError(f"reference attention kernel failed with cudaError {rc}")
+
+
+def fp64_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.ndarray:
+    """softmax(scale * q k^T) v in fp64 for [..., S, D] arrays (the
+    mathematical definition the reference's kernels approximate,
+    src/main.cpp:1027-1098): the ground truth for both sides."""
+    q, k, v = (np.asarray(x, dtype=np.float64) for x in (q, k, v))
+    s = np.einsum("...qd,...kd->...qk", q, k) * float(scale)
+    s -= s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("...qk,...kd->...qd", p, v)
+
+
 def ref_gpu_available() -> bool:
     return os.path.exists(REF_LIB)
 

@@ -10,6 +10,12 @@
 void launch_matmul_fp16(const void* input, const void* weight, void* output, int M, int N, int K);
 void launch_matmul_fp32(const float* input, const float* weight, float* output, int M, int N, int K);
 void launch_matmul_bf16(const void* input, const void* weight, void* output, int M, int N, int K);
+void launch_attention_fp32(const float* q, const float* k, const float* v, float* output, int B, int H, int S, int D,
+                           float scale);
+void launch_attention_fp16(const void* q, const void* k, const void* v, void* output, int B, int H, int S, int D,
+                           float scale);
+void launch_attention_bf16(const void* q, const void* k, const void* v, void* output, int B, int H, int S, int D,
+                           float scale);
 
 // dtype: 0 = fp16, 1 = bf16, 2 = fp32.  Launches on the legacy default stream
 // (as the reference does), waits for completion, returns the cudaError_t.
@@ -35,6 +41,23 @@ extern "C" __attribute__((visibility("default"))) int ref_matmul(int dtype, cons
     launch_matmul_fp16(A, B, C, M, N, K);
   } else if (dtype == 1) launch_matmul_bf16(A, B, C, M, N, K);
   else launch_matmul_fp32(static_cast<const float*>(A), static_cast<const float*>(B), static_cast<float*>(C), M, N, K);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return int(e);
+}
+
+// The reference's attention launchers (src/main.cpp:48-50) on device
+// pointers; synchronises and returns the cudaError_t.  The callers in
+// oracle.py only pass shapes these kernels handle (fp16: D = 128; fp32:
+// D % 4 == 0, D <= 128; bf16: S floats of shared memory).
+extern "C" __attribute__((visibility("default"))) int ref_attention(int dtype, const void* q, const void* k,
+                                                                     const void* v, void* o, int B, int H, int S,
+                                                                     int D, float scale) {
+  cudaGetLastError();
+  if (dtype == 0) launch_attention_fp16(q, k, v, o, B, H, S, D, scale);
+  else if (dtype == 1) launch_attention_bf16(q, k, v, o, B, H, S, D, scale);
+  else launch_attention_fp32(static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
+                             static_cast<float*>(o), B, H, S, D, scale);
   cudaError_t e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaGetLastError();
   return int(e);

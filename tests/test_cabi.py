@@ -16,6 +16,9 @@ REF_LAUNCHERS = [  # reference src/main.cpp:12-19, C++ linkage
     "_Z20launch_add_bias_fp16PvPKvii",
     "_Z20launch_add_bias_fp32PfPKfii",
     "_Z20launch_add_bias_bf16PvPKvii",
+    "_Z21launch_attention_fp32PKfS0_S0_Pfiiiif",  # src/main.cpp:48-50
+    "_Z21launch_attention_fp16PKvS0_S0_Pviiiif",
+    "_Z21launch_attention_bf16PKvS0_S0_Pviiiif",
 ]
 
 

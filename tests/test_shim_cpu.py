@@ -14,7 +14,7 @@ def raises(msg, fn, *a):
 
 
 def test_drop_in_module_names():
-    for name in ("linear", "bmm", "conv2d", "fp16_matmul", "bf16_matmul", "fp32_matmul"):
+    for name in ("linear", "bmm", "conv2d", "attention", "fp16_matmul", "bf16_matmul", "fp32_matmul"):
         assert getattr(cmpext3, name) is getattr(cx, name)
 
 
@@ -75,3 +75,15 @@ def test_host_matmul_argument_checks():
         host_matmul(torch.zeros(2, 3), torch.zeros(3, 4, dtype=torch.float16))
     with pytest.raises(ValueError, match="Contracting"):
         host_matmul(torch.zeros(2, 3), torch.zeros(4, 4))
+
+
+def test_attention_checks():
+    """Reference messages of custom_attention_forward (src/main.cpp:1034-1045)."""
+    q = torch.zeros(1, 2, 8, 4)
+    raises(r"Query must be 4D \(Batch, Head, Seq, Dim\)", cx.attention, torch.zeros(2, 8, 4), q, q)
+    raises("Key must be 4D", cx.attention, q, torch.zeros(2, 8, 4), q)
+    raises("Value must be 4D", cx.attention, q, q, torch.zeros(2, 8, 4))
+    raises("Key shape mismatch", cx.attention, q, torch.zeros(1, 2, 9, 4), q)
+    raises("Value shape mismatch", cx.attention, q, q, torch.zeros(1, 2, 8, 5))
+    raises("expects CUDA tensors", cx.attention, q, q, q)
+    raises("expects CUDA tensors", lambda: cx.attention(q, q, q, scale=0.5))

@@ -592,6 +592,12 @@ def run_ours(args):
     world, rank, local = dist_setup(args)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.attention is not None:
+        # profiling / spot runs of the attention workload alone (one GPU)
+        dt = {"fp16": torch.float16, "bf16": torch.bfloat16}[args.attention]
+        rec = attention_record(Timer(1, device, args.quick, args.hold), peaks()[0], args, device, dt)
+        print(json.dumps(rec), flush=True)
+        return 0
     cfg = CONFIGS[args.config]
     metric, unit = metric_of(cfg)
     r0, r1 = shard_rows(cfg.M, world, rank)
@@ -797,6 +803,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="profiling mode: only W warm-up + K timed steps (no clock sampling, e2e or CPU legs)")
+    ap.add_argument("--attention", default=None, choices=["fp16", "bf16"],
+                    help="measure only cmpext3.attention on the reference's benchmark shape (8x8x1024x128)")
     ap.add_argument("--rows", type=int, default=None, help="override this rank's M rows (profiling small cases)")
     ap.add_argument("--f32-path", default="tf32x3", choices=["tf32x3", "bf16x3"],
                     help="fp32 configs: 3xTF32 (default) or the opt-in bf16x3 split")

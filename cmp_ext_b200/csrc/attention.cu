@@ -68,6 +68,15 @@ __device__ __forceinline__ void rec_err(int* err, volatile int* abort, int code)
   atomicCAS(err, 0, code);
 }
 
+// 2^x with the hardware's approximate base-2 exponential (ex2.approx,
+// relative error ~2^-22; results below 2^-126 flush to zero, which a softmax
+// weight that small does not need).  2^-inf = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -287,45 +296,69 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         const uint32_t s_addr = t_lane + uint32_t(b * 128);
         const int kv0 = j * 128;
-        float mx = -INFINITY;
+        // A block lies wholly inside the keys except possibly the last one.
+        const bool full = kv0 + 128 <= p.S;
+        const float sl = p.scale_log2;
+        // pass 1: the row maximum over all 128 keys of the block, on the raw
+        // scores (one scaling at the end; the order flips for a negative scale)
+        float mx_hi = -INFINITY, mx_lo = INFINITY;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t x[16];
-          tmem_ld_32x32b_x16(s_addr + c * 16, x);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t x[64];
+          tmem_ld_32x32b_x32(s_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+          tmem_ld_32x32b_x32(s_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
           tmem_ld_wait();
+          if (full) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (kv0 + c * 16 + i < p.S) mx = fmaxf(mx, __uint_as_float(x[i]) * p.scale_log2);
-        }
-        m_new = fmaxf(m_run, mx);
-        float sum = 0.0f;
-        // this thread's keys [64h, 64h + 64) are chunk h of P's two 64-key chunks
-        uint8_t* prow = sP + b * Cfg::P_BYTES + h * 16384 + r * 128;
+            for (int i = 0; i < 64; ++i) {
+              mx_hi = fmaxf(mx_hi, __uint_as_float(x[i]));
+              mx_lo = fminf(mx_lo, __uint_as_float(x[i]));
+            }
+          } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t x[16];
-          const int k0 = h * 64 + c * 16;
-          tmem_ld_32x32b_x16(s_addr + k0, x);
-          tmem_ld_wait();
-          float pv[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            pv[i] = (kv0 + k0 + i < p.S) ? exp2f(fmaf(__uint_as_float(x[i]), p.scale_log2, -m_new)) : 0.0f;
-            sum += pv[i];
+            for (int i = 0; i < 64; ++i)
+              if (kv0 + c * 64 + i < p.S) {
+                mx_hi = fmaxf(mx_hi, __uint_as_float(x[i]));
+                mx_lo = fminf(mx_lo, __uint_as_float(x[i]));
+              }
           }
-          // keys [k0, k0 + 16): 16-byte units 2c and 2c + 1 of the row's 128 bytes
+        }
+        m_new = fmaxf(m_run, sl >= 0.0f ? mx_hi * sl : mx_lo * sl);
+        float sum = 0.0f;
+        // pass 2: this thread's keys [64h, 64h + 64), which are chunk h of
+        // P's two 64-key chunks
+        uint8_t* prow = sP + b * Cfg::P_BYTES + h * 16384 + r * 128;
+        {
+          uint32_t x[64];
+          tmem_ld_32x32b_x32(s_addr + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+          tmem_ld_32x32b_x32(s_addr + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+          tmem_ld_wait();
+          float pv[64];
+          if (full) {
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
+            for (int i = 0; i < 64; ++i) {
+              pv[i] = ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new));
+              sum += pv[i];
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+              pv[i] = (kv0 + h * 64 + i < p.S) ? ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new)) : 0.0f;
+              sum += pv[i];
+            }
+          }
+          // 16-byte unit u of the row's 128 bytes holds keys [8u, 8u + 8)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
             uint4 q;
-            q.x = pack2(pv[g * 8 + 0], pv[g * 8 + 1], (T*)nullptr);
-            q.y = pack2(pv[g * 8 + 2], pv[g * 8 + 3], (T*)nullptr);
-            q.z = pack2(pv[g * 8 + 4], pv[g * 8 + 5], (T*)nullptr);
-            q.w = pack2(pv[g * 8 + 6], pv[g * 8 + 7], (T*)nullptr);
-            const int u = c * 2 + g;
+            q.x = pack2(pv[u * 8 + 0], pv[u * 8 + 1], (T*)nullptr);
+            q.y = pack2(pv[u * 8 + 2], pv[u * 8 + 3], (T*)nullptr);
+            q.z = pack2(pv[u * 8 + 4], pv[u * 8 + 5], (T*)nullptr);
+            q.w = pack2(pv[u * 8 + 6], pv[u * 8 + 7], (T*)nullptr);
             *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = q;
           }
         }
-        l = l * exp2f(m_run - m_new) + sum;
+        l = l * ex2_approx(m_run - m_new) + sum;
         m_run = m_new;
         tc_fence_before();
         mbar_arrive(&s_empty[b]);   // S buffer may be overwritten by QK_{j+2}
@@ -339,7 +372,7 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        const float beta = exp2f(m_prev - m_hist);  // 0 while nothing has been folded
+        const float beta = ex2_approx(m_prev - m_hist);  // 0 while nothing has been folded
 #pragma unroll
         for (int c = 0; c < DH / 16; ++c) {
           uint32_t x[16];

@@ -527,6 +527,16 @@ unsigned epilogue_sleep_ns() {
   return unsigned(v);
 }
 
+int tc2_group_m() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("CMPX_TC_GROUP_M");
+    const long x = e != nullptr ? std::strtol(e, nullptr, 10) : 8;
+    v = x < 1 ? 1 : (x > 64 ? 64 : int(x));
+  }
+  return v;
+}
+
 int* device_error_word() {
   DeviceState* d = nullptr;
   return device_state(&d) == CMPX_OK ? d->err_word : nullptr;

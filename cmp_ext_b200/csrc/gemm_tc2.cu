@@ -526,7 +526,7 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   p.stride_c = g.sc;
   p.tiles_m = int((g.M + 255) / 256);
   p.tiles_n = int((g.N + PN - 1) / PN);
-  p.group_m = 8;
+  p.group_m = tc2_group_m();
   p.a_bcast = g.a_bcast;
   p.bias_m = g.bias_m;
   p.peers = g.peers;

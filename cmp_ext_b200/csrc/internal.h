@@ -142,6 +142,9 @@ bool pdl_enabled();
 // Sleep between polls of a tile kernel's epilogue while it waits for the
 // next accumulator (CMPX_EPI_SLEEP_NS, default 0 = spin).
 unsigned epilogue_sleep_ns();
+// Pair tiles per M group of the CTA-pair kernel's raster (CMPX_TC_GROUP_M,
+// default 8): the tiles of one group share A rows and walk B's columns.
+int tc2_group_m();
 // Fills `attr` (one slot) and cfg.attrs / cfg.numAttrs for a PDL launch, or
 // leaves cfg without attributes when PDL is off.
 inline void apply_pdl(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int used) {

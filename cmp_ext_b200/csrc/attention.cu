@@ -15,8 +15,8 @@
 //     O_j = P_j V_j into one of two D-column TMEM buffers (A = P from shared
 //     memory, B = V_j N-major), ordered QK_0, QK_1, PV_0, QK_2, PV_1, ... so
 //     one score block is computed while the previous one is in softmax;
-//   * warps 2-9 (two threads per query row, each owning half of the keys
-//     of a block and half of the output columns): read S_j from TMEM, keep
+//   * warps 2.. (two threads per query row by default, each owning half of
+//     the keys of a block and half of the output columns): read S_j from TMEM, keep
 //     the running row maximum m (both threads of a row read the whole row,
 //     so they agree on it without exchanging anything) and a partial sum l
 //     in fp32 (base-2 exponent with scale * log2 e folded in), write their
@@ -36,6 +36,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdio>
+#include <cstdlib>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -45,15 +46,18 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int D>
+template <int D, int TPR>
 struct AttnCfg {
+  static constexpr int THREADS = 64 + 128 * TPR;     // TMA warp, MMA warp, TPR threads per query row
+  static constexpr int SMX = 128 * TPR;              // softmax threads
   static constexpr int QCH = D / 64;                 // 64-element (128-byte) chunks of D
   static constexpr int TILE_BYTES = 128 * D * 2;     // 128 rows x D x 2 B
   static constexpr int P_BYTES = 128 * 128 * 2;      // P block: 128 rows x 128 keys x 2 B
   static constexpr int KST = 2, VST = 2;             // ring depths
-  static constexpr size_t SMEM = size_t(TILE_BYTES) * (1 + KST + VST) + 2 * P_BYTES + 1024 + 256 + 1024;
+  static constexpr size_t SMEM = size_t(TILE_BYTES) * (1 + KST + VST) + 2 * P_BYTES + 1024 + 256;
   static constexpr uint32_t TMEM_COLS = 512;         // S0 S1 (128 each) then O0 O1 (D each)
   static_assert(D == 64 || D == 128, "tensor-core attention supports D = 64 or 128");
+  static_assert(TPR == 2 || TPR == 4, "two or four threads per query row");
 };
 
 struct AttnParams {
@@ -86,11 +90,11 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int FMT, int D>
-__global__ void __launch_bounds__(320, 1)
+template <int FMT, int D, int TPR>
+__global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  using Cfg = AttnCfg<D>;
+  using Cfg = AttnCfg<D, TPR>;
   using T = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
   constexpr uint32_t IDESC_QK = make_idesc(uint32_t(FMT), 0u, 0u, 128, 128);
   constexpr uint32_t IDESC_PV = make_idesc(uint32_t(FMT), 0u, 1u, 128, D);
@@ -114,9 +118,11 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* o_full = p_full + 2;           // [2]
   uint64_t* o_empty = o_full + 2;          // [2]
   uint64_t* drain = o_empty + 2;
-  uint64_t* l_bar = drain + 1;             // the 256 partial row sums are in l_part
-  float* l_part = reinterpret_cast<float*>(l_bar + 1);  // [2][128]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(l_part + 256);
+  uint64_t* l_bar = drain + 1;             // the partial row sums are in l_part
+  // [TPR][128] partial row sums, written after the last PV MMA has read the
+  // P buffers, so they reuse P's space
+  float* l_part = reinterpret_cast<float*>(sP);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(l_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -136,13 +142,13 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 256);
-      mbar_init(&p_full[i], 256);
+      mbar_init(&s_empty[i], Cfg::SMX);
+      mbar_init(&p_full[i], Cfg::SMX);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 256);
+      mbar_init(&o_empty[i], Cfg::SMX);
     }
     mbar_init(drain, 1);
-    mbar_init(l_bar, 256);
+    mbar_init(l_bar, Cfg::SMX);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -269,10 +275,11 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax + output (warps 2..9)
-    constexpr int DH = D / 2;        // output columns per thread
+    // ------------------------------------------------------------ softmax + output (warps 2..)
+    constexpr int DH = D / TPR;      // output columns per thread
+    constexpr int KPT = 128 / TPR;   // keys of a block per thread
     const int qw = warp & 3;         // TMEM lane quarter this warp may access
-    const int h = (warp - 2) >> 2;   // which half of the keys / output columns
+    const int h = (warp - 2) >> 2;   // which share of the keys / output columns
     const int r = qw * 32 + lane;    // row of this CTA's 128
     const uint32_t t_lane = tmem_base + (uint32_t(qw * 32) << 16);
     float o[DH];
@@ -303,21 +310,20 @@ __global__ void __launch_bounds__(320, 1)
         // scores (one scaling at the end; the order flips for a negative scale)
         float mx_hi = -INFINITY, mx_lo = INFINITY;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t x[64];
-          tmem_ld_32x32b_x32(s_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
-          tmem_ld_32x32b_x32(s_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+        for (int c = 0; c < 4; ++c) {
+          uint32_t x[32];
+          tmem_ld_32x32b_x32(s_addr + c * 32, x);
           tmem_ld_wait();
           if (full) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
+            for (int i = 0; i < 32; ++i) {
               mx_hi = fmaxf(mx_hi, __uint_as_float(x[i]));
               mx_lo = fminf(mx_lo, __uint_as_float(x[i]));
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (kv0 + c * 64 + i < p.S) {
+            for (int i = 0; i < 32; ++i)
+              if (kv0 + c * 32 + i < p.S) {
                 mx_hi = fmaxf(mx_hi, __uint_as_float(x[i]));
                 mx_lo = fminf(mx_lo, __uint_as_float(x[i]));
               }
@@ -325,36 +331,39 @@ __global__ void __launch_bounds__(320, 1)
         }
         m_new = fmaxf(m_run, sl >= 0.0f ? mx_hi * sl : mx_lo * sl);
         float sum = 0.0f;
-        // pass 2: this thread's keys [64h, 64h + 64), which are chunk h of
-        // P's two 64-key chunks
-        uint8_t* prow = sP + b * Cfg::P_BYTES + h * 16384 + r * 128;
-        {
-          uint32_t x[64];
-          tmem_ld_32x32b_x32(s_addr + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
-          tmem_ld_32x32b_x32(s_addr + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+        // pass 2: this thread's keys [KPT h, KPT (h + 1)): 64-key chunk
+        // (KPT h) / 64 of P, 16-byte units from ((KPT h) % 64) / 8 on
+        const int key0 = h * KPT;
+        uint8_t* prow = sP + b * Cfg::P_BYTES + (key0 >> 6) * 16384 + r * 128;
+        const int u0 = (key0 & 63) >> 3;
+#pragma unroll
+        for (int c = 0; c < KPT / 32; ++c) {
+          uint32_t x[32];
+          tmem_ld_32x32b_x32(s_addr + key0 + c * 32, x);
           tmem_ld_wait();
-          float pv[64];
+          float pv[32];
           if (full) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
+            for (int i = 0; i < 32; ++i) {
               pv[i] = ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new));
               sum += pv[i];
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-              pv[i] = (kv0 + h * 64 + i < p.S) ? ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new)) : 0.0f;
+            for (int i = 0; i < 32; ++i) {
+              pv[i] = (kv0 + key0 + c * 32 + i < p.S) ? ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new)) : 0.0f;
               sum += pv[i];
             }
           }
-          // 16-byte unit u of the row's 128 bytes holds keys [8u, 8u + 8)
+          // 16-byte unit u of the row's 128 bytes holds keys [8u, 8u + 8) of the chunk
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
+          for (int g = 0; g < 4; ++g) {
             uint4 q;
-            q.x = pack2(pv[u * 8 + 0], pv[u * 8 + 1], (T*)nullptr);
-            q.y = pack2(pv[u * 8 + 2], pv[u * 8 + 3], (T*)nullptr);
-            q.z = pack2(pv[u * 8 + 4], pv[u * 8 + 5], (T*)nullptr);
-            q.w = pack2(pv[u * 8 + 6], pv[u * 8 + 7], (T*)nullptr);
+            q.x = pack2(pv[g * 8 + 0], pv[g * 8 + 1], (T*)nullptr);
+            q.y = pack2(pv[g * 8 + 2], pv[g * 8 + 3], (T*)nullptr);
+            q.z = pack2(pv[g * 8 + 4], pv[g * 8 + 5], (T*)nullptr);
+            q.w = pack2(pv[g * 8 + 6], pv[g * 8 + 7], (T*)nullptr);
+            const int u = u0 + c * 4 + g;
             *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = q;
           }
         }
@@ -397,7 +406,10 @@ __global__ void __launch_bounds__(320, 1)
     if (!ok) {
       if (lane == 0) rec_err(p.err, abort_flag, kDevTimeoutAccFull);
     } else if (q0 + r < p.S) {
-      const float inv = 1.0f / (l_part[r] + l_part[128 + r]);
+      float lsum = 0.0f;
+#pragma unroll
+      for (int t = 0; t < TPR; ++t) lsum += l_part[t * 128 + r];
+      const float inv = 1.0f / lsum;
       T* orow = reinterpret_cast<T*>(p.O) + (size_t(bh) * p.S + q0 + r) * D + h * DH;
 #pragma unroll
       for (int g = 0; g < DH / 8; ++g) {
@@ -489,11 +501,11 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const T* __restrict
   }
 }
 
-template <int FMT, int D>
+template <int FMT, int D, int TPR>
 cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int64_t BH, int64_t S, float scale,
                       int* err, cudaStream_t s) {
-  using Cfg = AttnCfg<D>;
-  auto kern = attention_tc_kernel<FMT, D>;
+  using Cfg = AttnCfg<D, TPR>;
+  auto kern = attention_tc_kernel<FMT, D, TPR>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
   static unsigned long long smem_set = 0;
   cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
@@ -512,7 +524,7 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   p.err = err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(BH * p.qtiles));
-  cfg.blockDim = dim3(320);
+  cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -532,6 +544,19 @@ cudaError_t launch_simt_attn(const void* Q, const void* K, const void* V, void* 
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Softmax threads per query row of the tensor-core kernel: 2 by default,
+// 4 with CMPX_ATTN_TPR=4 (twice the warps to hide latency, but every thread
+// still reads the whole score row for the maximum; measured on a B200 on
+// 8x8x1024x128 fp16: 503 TFLOP/s with 2, 477 with 4).
+int attention_threads_per_row() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("CMPX_ATTN_TPR");
+    v = (e != nullptr && e[0] == '4') ? 4 : 2;
+  }
+  return v;
+}
 
 }  // namespace
 
@@ -566,12 +591,22 @@ extern "C" int cmpx_attention(int dtype, const void* Q, const void* K, const voi
   cudaError_t e;
   if (pth == CMPX_PATH_TC) {
     if (BH * ((S + 127) / 128) > 0x7fffffffLL) return CMPX_ERR_UNSUPPORTED;
-    if (dtype == CMPX_F16)
-      e = D == 64 ? launch_tc<0, 64>(Q, K, V, O, BH, S, scale, err, stream)
-                  : launch_tc<0, 128>(Q, K, V, O, BH, S, scale, err, stream);
-    else
-      e = D == 64 ? launch_tc<1, 64>(Q, K, V, O, BH, S, scale, err, stream)
-                  : launch_tc<1, 128>(Q, K, V, O, BH, S, scale, err, stream);
+    const bool four = attention_threads_per_row() == 4;
+    if (dtype == CMPX_F16) {
+      if (D == 64)
+        e = four ? launch_tc<0, 64, 4>(Q, K, V, O, BH, S, scale, err, stream)
+                 : launch_tc<0, 64, 2>(Q, K, V, O, BH, S, scale, err, stream);
+      else
+        e = four ? launch_tc<0, 128, 4>(Q, K, V, O, BH, S, scale, err, stream)
+                 : launch_tc<0, 128, 2>(Q, K, V, O, BH, S, scale, err, stream);
+    } else {
+      if (D == 64)
+        e = four ? launch_tc<1, 64, 4>(Q, K, V, O, BH, S, scale, err, stream)
+                 : launch_tc<1, 64, 2>(Q, K, V, O, BH, S, scale, err, stream);
+      else
+        e = four ? launch_tc<1, 128, 4>(Q, K, V, O, BH, S, scale, err, stream)
+                 : launch_tc<1, 128, 2>(Q, K, V, O, BH, S, scale, err, stream);
+    }
   } else {
     if ((BH * S + 3) / 4 > 0x7fffffffLL) return CMPX_ERR_UNSUPPORTED;
     e = dtype == CMPX_F16    ? launch_simt_attn<__half>(Q, K, V, O, BH, S, D, scale, stream)

@@ -392,10 +392,6 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
       st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, uint32_t(pair_n / 2))
                       : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
       if (st != CMPX_OK) return st;
-      CUtensorMap tBh = tB;
-      if (g.b_kmajor && (st = encode_3d(&tBh, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64,
-                                        uint32_t(pair_n / 4))) != CMPX_OK)
-        return st;
       if (g.peers.n > 0) {
         // Output also goes to peer GPUs: staged TMA stores (bulk NVLink writes).
         OutMaps om{};
@@ -403,9 +399,9 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
         if ((st = encode_out_map(&om.m[0], g, g.C)) != CMPX_OK) return st;
         for (int i = 0; i < g.peers.n; ++i)
           if ((st = encode_out_map(&om.m[1 + i], g, g.peers.base[i])) != CMPX_OK) return st;
-        return cuda_status(launch_tc2_f16(g, tA, tB, tBh, pair_n, ws, d->info, d->err_word, s, &om));
+        return cuda_status(launch_tc2_f16(g, tA, tB, pair_n, ws, d->info, d->err_word, s, &om));
       }
-      return cuda_status(launch_tc2_f16(g, tA, tB, tBh, pair_n, ws, d->info, d->err_word, s));
+      return cuda_status(launch_tc2_f16(g, tA, tB, pair_n, ws, d->info, d->err_word, s));
     }
     st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 256)
                     : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
@@ -508,7 +504,7 @@ int run_gemm_flagged(const cmpx_gemm_args* args, int* flags, int flag_tiles, cud
   st = g.b_kmajor ? encode_3d(&tB, g.dtype, g.B, g.K, g.N, g.batch, g.ldb, g.sb, 64, 128)
                   : encode_3d(&tB, g.dtype, g.B, g.N, g.K, g.batch, g.ldb, g.sb, 64, 64);
   if (st != CMPX_OK) return st;
-  return cuda_status(launch_tc2_f16(g, tA, tB, tB, 256, nullptr, d->info, d->err_word, s));
+  return cuda_status(launch_tc2_f16(g, tA, tB, 256, nullptr, d->info, d->err_word, s));
 }
 
 // CMPX_PDL=0 turns programmatic dependent launch off (A/B measurements).
@@ -529,15 +525,6 @@ unsigned epilogue_sleep_ns() {
     v = x < 0 ? 0 : (x > 100000 ? 100000 : x);
   }
   return unsigned(v);
-}
-
-bool tail_split_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("CMPX_TC_TAIL_SPLIT");
-    v = (e != nullptr && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
 }
 
 int tc2_group_m() {

@@ -43,7 +43,6 @@ struct Tc2Params {
   // (sk_units = sk_tiles * k-blocks) are split evenly over all pairs.
   int dp_tiles, sk_tiles;
   int sk_pairs;  // pairs sharing the stream-K units: min(pairs, sk_units), so none is empty
-  int split_tiles;  // tail tiles computed as two half-width items (see work_item)
   long long sk_units;
   float* ws;      // [pair][slot 2][rank 2][128][PN] fp32 partials of split tiles
   int* counters;  // [sk tile][rank 2][epilogue warp 4], zero on entry and exit
@@ -60,7 +59,6 @@ struct Tc2Params {
 // skt >= 0 marks a stream-K tile (its index among the split tiles).
 struct WorkItem {
   int tile, kb0, kb1, skt;
-  int half;  // -1: the whole 256 x PN tile; 0 / 1: its left / right PN/2 columns
 };
 
 __device__ __forceinline__ long long sk_begin(long long g, long long U, long long P) { return g * U / P; }
@@ -69,25 +67,10 @@ __device__ __forceinline__ long long sk_owner(long long u, long long U, long lon
 // The item-th work item of pair `c` (false when there is none): first its
 // whole data-parallel tiles, then the pieces of its stream-K unit range cut
 // at tile boundaries.  Every role of both CTAs walks the same sequence.
-// With split_tiles > 0 (whole tiles only, no stream-K) the last split_tiles
-// data-parallel tiles -- the partial last wave -- are computed as 2 *
-// split_tiles half-width items, one per pair, so the tail wave takes half as
-// long.
 __device__ __forceinline__ bool work_item(const Tc2Params& p, int c, int P, int num_kb, int item, WorkItem& w) {
-  const int n_whole = p.dp_tiles - p.split_tiles;
-  const int n_dp = c < n_whole ? (n_whole - c + P - 1) / P : 0;
-  w.half = -1;
+  const int n_dp = c < p.dp_tiles ? (p.dp_tiles - c + P - 1) / P : 0;
   if (item < n_dp) {
     w.tile = c + item * P;
-    w.kb0 = 0;
-    w.kb1 = num_kb;
-    w.skt = -1;
-    return true;
-  }
-  if (p.split_tiles > 0) {
-    if (item > n_dp || c >= 2 * p.split_tiles) return false;
-    w.tile = n_whole + (c >> 1);
-    w.half = c & 1;
     w.kb0 = 0;
     w.kb1 = num_kb;
     w.skt = -1;
@@ -122,7 +105,6 @@ struct Tc2Cfg {
   static constexpr int STAGING_BYTES = TMA_OUT ? 4 * 2 * 2048 : 0;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + STAGING_BYTES + 1024 + 512;
   static constexpr uint32_t IDESC = make_idesc(uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, 256, PN);
-  static constexpr uint32_t IDESC_HALF = make_idesc(uint32_t(FMT), 0u, B_KMAJOR ? 0u : 1u, 256, PN / 2);
   static_assert(BH % 64 == 0, "B half must be whole 64-column chunks");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
 };
@@ -230,8 +212,7 @@ __device__ __forceinline__ void pack_row32_16(const uint32_t (&r)[32], const T* 
 template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT, bool STREAMK>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmBh, const Tc2Params p,
-                    const __grid_constant__ OutMaps om) {
+                    const Tc2Params p, const __grid_constant__ OutMaps om) {
   using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES, TMA_OUT>;
   using OutT = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
 
@@ -289,10 +270,7 @@ __global__ void __launch_bounds__(192, 1)
         int b, tm, tn;
         decode_tile2(w.tile, p, b, tm, tn);
         const int m0 = tm * 256 + int(rank) * 128;
-        // this CTA's share of the item's columns: BH of a whole tile, BH / 2 of a half
-        const int bw = w.half < 0 ? Cfg::BH : Cfg::BH / 2;
-        const int n0 = tn * PN + (w.half < 0 ? 0 : w.half * (PN / 2)) + int(rank) * bw;
-        const uint32_t stage_tx = 2u * uint32_t(Cfg::A_BYTES + bw * 128);
+        const int n0 = tn * PN + int(rank) * Cfg::BH;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
             record_error2(p.err, abort_flag, kDevTimeoutEmpty);
@@ -300,15 +278,16 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           const uint32_t full_leader = mapa_cluster(&full_bar[stage], 0);
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], stage_tx);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
           uint8_t* sA = smem + size_t(stage) * Cfg::STAGE_BYTES;
           uint8_t* sB = sA + Cfg::A_BYTES;
           const int k0 = kb * Cfg::BK;
           tma_load_3d_pair(sA, &tmA, full_leader, k0, m0, p.a_bcast ? 0 : b);
           if (B_KMAJOR) {
-            tma_load_3d_pair(sB, w.half < 0 ? &tmB : &tmBh, full_leader, k0, n0, b);
+            tma_load_3d_pair(sB, &tmB, full_leader, k0, n0, b);
           } else {
-            for (int j = 0; j < bw / 64; ++j) tma_load_3d_pair(sB + j * 8192, &tmB, full_leader, n0 + 64 * j, k0, b);
+#pragma unroll
+            for (int j = 0; j < Cfg::BH / 64; ++j) tma_load_3d_pair(sB + j * 8192, &tmB, full_leader, n0 + 64 * j, k0, b);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -354,8 +333,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t adesc = make_sdesc_sw128(a_addr + ks * 32, 16, 1024);
             const uint64_t bdesc = B_KMAJOR ? make_sdesc_sw128(b_addr + ks * 32, 16, 1024)
                                             : make_sdesc_sw128(b_addr + ks * 2048, 8192, 1024);
-            mma_f16_pair(d_tmem, adesc, bdesc, w.half < 0 ? Cfg::IDESC : Cfg::IDESC_HALF,
-                         (kb != w.kb0 || ks != 0) ? 1u : 0u);
+            mma_f16_pair(d_tmem, adesc, bdesc, Cfg::IDESC, (kb != w.kb0 || ks != 0) ? 1u : 0u);
           }
           mma_commit_pair_mc(&empty_bar[stage], 0x3);  // both CTAs' slots are free once these retire
           if (++stage == STAGES) {
@@ -412,10 +390,8 @@ __global__ void __launch_bounds__(192, 1)
         const int slot = (w.skt == first_skt) ? 0 : 1;
         part = p.ws + ((size_t(cluster_id) * 2 + slot) * 2 + rank) * 128 * PN + size_t(lrow) * PN;
       }
-      const int ncol0 = tn * PN + (w.half < 0 ? 0 : w.half * (PN / 2));  // the item's first column
-      const int nchunks = (w.half < 0 ? PN : PN / 2) / 32;
 #pragma unroll 1
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = 0; c < PN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
@@ -427,19 +403,19 @@ __global__ void __launch_bounds__(192, 1)
             if (lane == 0) bulk_wait_read1();  // the store that last read this buffer is done with it
             __syncwarp();
             uint4 o[4];
-            pack_row32_16<OutT>(r, colb, rowb, ncol0 + c * 32, p.N, o);
+            pack_row32_16<OutT>(r, colb, rowb, tn * PN + c * 32, p.N, o);
 #pragma unroll
             for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stg + lane * 64 + j * 16) = o[j];
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
               const int row0 = tm * 256 + int(rank) * 128 + q * 32;
-              for (int d = 0; d < om.n; ++d) tma_store_3d(&om.m[d], stg, ncol0 + c * 32, row0, b);
+              for (int d = 0; d < om.n; ++d) tma_store_3d(&om.m[d], stg, tn * PN + c * 32, row0, b);
               bulk_commit();
             }
             ++chunk_seq;
           } else {
-            if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, ncol0 + c * 32, p.N, r, p.peers, row_off);
+            if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r, p.peers, row_off);
           }
         } else {
           float4* dst = reinterpret_cast<float4*>(part + c * 32);
@@ -531,7 +507,7 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int FMT, bool B_KMAJOR, int PN, int STAGES, bool TMA_OUT, bool STREAMK>
-cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tBh, void* ws,
+cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
                            const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps& om) {
   using Cfg = Tc2Cfg<FMT, B_KMAJOR, PN, STAGES, TMA_OUT>;
   auto kern = gemm_tc2_kernel<FMT, B_KMAJOR, PN, STAGES, TMA_OUT, STREAMK>;
@@ -569,19 +545,11 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   if (STREAMK && ws != nullptr && rem != 0) sk = total >= pairs ? rem + pairs : total;
   p.dp_tiles = int(total - sk);
   p.sk_tiles = int(sk);
-  // Half-width tail: when the last, partial wave fills at most half the
-  // pairs, its tiles run as two half-width items each (whole-tile launches
-  // with 256-column pair tiles and no column-progress flags).
-  p.split_tiles = (!STREAMK && PN == 256 && g.col_flags == nullptr && tail_split_enabled() && rem != 0 &&
-                   2 * rem <= pairs)
-                      ? int(rem)
-                      : 0;
   p.sk_units = sk * num_kb;
   p.sk_pairs = int(p.sk_units < pairs ? p.sk_units : pairs);
   p.counters = reinterpret_cast<int*>(ws);
   p.ws = ws != nullptr ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes) : nullptr;
-  long long clusters = sk > 0 ? pairs : (total < pairs ? total : pairs);
-  if (p.split_tiles > 0 && total < pairs) clusters = 2LL * p.split_tiles;
+  const long long clusters = sk > 0 ? pairs : (total < pairs ? total : pairs);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(2 * clusters), 1, 1);
@@ -594,19 +562,19 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   apply_pdl(cfg, attr, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tBh, p, om);
+  e = cudaLaunchKernelEx(&cfg, kern, tA, tB, p, om);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 template <int FMT, bool B_KMAJOR, int PN, int STAGES>
-cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tBh, void* ws,
+cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, void* ws,
                             const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om) {
   // Peer outputs (staged TMA stores) run whole tiles only.
-  if (om != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, true, false>(g, tA, tB, tBh, nullptr, dev, dev_err, s, *om);
+  if (om != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, true, false>(g, tA, tB, nullptr, dev, dev_err, s, *om);
   static OutMaps none{};
-  if (ws != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, true>(g, tA, tB, tBh, ws, dev, dev_err, s, none);
-  return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, false>(g, tA, tB, tBh, nullptr, dev, dev_err, s, none);
+  if (ws != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, true>(g, tA, tB, ws, dev, dev_err, s, none);
+  return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, false>(g, tA, tB, nullptr, dev, dev_err, s, none);
 }
 
 }  // namespace
@@ -622,21 +590,20 @@ size_t tc2_workspace_bytes(const Gemm& g, int pair_n, const DeviceInfo& dev) {
   return kSkinnyCounterBytes + size_t(pairs) * 2 * 2 * 128 * size_t(pair_n) * 4;
 }
 
-cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tBh,
-                           int pair_n, void* ws,
+cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n, void* ws,
                            const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om) {
   if (pair_n == 256) {
     if (g.dtype == CMPX_F16)
-      return g.b_kmajor ? launch_tc2_impl<0, true, 256, 6>(g, tA, tB, tBh, ws, dev, dev_err, s, om)
-                        : launch_tc2_impl<0, false, 256, 6>(g, tA, tB, tBh, ws, dev, dev_err, s, om);
-    return g.b_kmajor ? launch_tc2_impl<1, true, 256, 6>(g, tA, tB, tBh, ws, dev, dev_err, s, om)
-                      : launch_tc2_impl<1, false, 256, 6>(g, tA, tB, tBh, ws, dev, dev_err, s, om);
+      return g.b_kmajor ? launch_tc2_impl<0, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om)
+                        : launch_tc2_impl<0, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om);
+    return g.b_kmajor ? launch_tc2_impl<1, true, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om)
+                      : launch_tc2_impl<1, false, 256, 6>(g, tA, tB, ws, dev, dev_err, s, om);
   }
   if (g.dtype == CMPX_F16)
-    return g.b_kmajor ? launch_tc2_impl<0, true, 128, 8>(g, tA, tB, tBh, ws, dev, dev_err, s, om)
-                      : launch_tc2_impl<0, false, 128, 8>(g, tA, tB, tBh, ws, dev, dev_err, s, om);
-  return g.b_kmajor ? launch_tc2_impl<1, true, 128, 8>(g, tA, tB, tBh, ws, dev, dev_err, s, om)
-                    : launch_tc2_impl<1, false, 128, 8>(g, tA, tB, tBh, ws, dev, dev_err, s, om);
+    return g.b_kmajor ? launch_tc2_impl<0, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om)
+                      : launch_tc2_impl<0, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om);
+  return g.b_kmajor ? launch_tc2_impl<1, true, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om)
+                    : launch_tc2_impl<1, false, 128, 8>(g, tA, tB, ws, dev, dev_err, s, om);
 }
 
 }  // namespace cmpx

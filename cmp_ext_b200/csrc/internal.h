@@ -76,10 +76,7 @@ size_t tc2_workspace_bytes(const Gemm& g, int pair_n, const DeviceInfo& dev);
 // om: when non-null, the epilogue stages each 32 x 32 output chunk in shared
 // memory and writes it with TMA stores to every map in om (used when the
 // output also goes to peer GPUs: bulk writes instead of 16-byte stores).
-// tBh: map of B for the half-width tail items -- the same as tB for a [K,N]
-// B, box {64, pair_n / 4} for an [N,K] B.
-cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tBh,
-                           int pair_n, void* ws,
+cudaError_t launch_tc2_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tB, int pair_n, void* ws,
                            const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om = nullptr);
 
 // 3xTF32 tensor-core kernel for fp32: tA/tA2 map the tf32 hi/lo splits of A,
@@ -148,8 +145,6 @@ unsigned epilogue_sleep_ns();
 // Pair tiles per M group of the CTA-pair kernel's raster (CMPX_TC_GROUP_M,
 // default 8): the tiles of one group share A rows and walk B's columns.
 int tc2_group_m();
-// Half-width tail items in the CTA-pair kernel (on unless CMPX_TC_TAIL_SPLIT=0).
-bool tail_split_enabled();
 // Fills `attr` (one slot) and cfg.attrs / cfg.numAttrs for a PDL launch, or
 // leaves cfg without attributes when PDL is off.
 inline void apply_pdl(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int used) {

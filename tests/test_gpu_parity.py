@@ -403,52 +403,3 @@ def test_gather_ce_local_peers(cuda, shape, groups, nstreams):
     st = cabi.lib().cmpx_gemm_gather_ce(ctypes.byref(cabi.gemm_args(A[:64], B, small)), pp, 3, flags.data_ptr(),
                                         groups, 4, torch.cuda.current_stream().cuda_stream, cs, nstreams)
     assert st == cabi.ERR_UNSUPPORTED
-
-
-# ------------------------------------------------------------ half-width tail items
-# Pair-tile counts whose last wave fills at most half of the 74 SM pairs, so
-# the CTA-pair kernel runs those tiles as two half-width items: 256 tiles
-# (3 waves + 34), 8 tiles (all tail), 80 tiles (1 wave + 6), ragged edges.
-TAIL_SHAPES = [(2048, 8192, 512), (512, 1024, 256), (2560, 2048, 128), (500, 1000, 264), (4096, 4096, 64)]
-
-
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("b_layout", [cabi.B_KN, cabi.B_NK])
-@pytest.mark.parametrize("shape", TAIL_SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_pair_kernel_tail_split(cuda, dtype, b_layout, shape):
-    M, N, K = shape
-    check_case(M, N, K, dtype, b_layout=b_layout, path=cabi.PATH_TC, oracle=M * N * K <= 2 ** 28)
-
-
-def test_pair_kernel_tail_split_bits_match_whole_tiles(cuda, tmp_path):
-    """A half-width item accumulates every output element over the same K
-    order as a whole tile: the output is bit-identical with the split
-    switched off (CMPX_TC_TAIL_SPLIT=0, read once per process, so the second
-    run is a child process)."""
-    import os
-    import subprocess
-    import sys
-
-    script = tmp_path / "run.py"
-    script.write_text(
-        "import sys, torch\n"
-        f"sys.path.insert(0, {cabi.REPO!r})\n"
-        "import cmp_ext_b200 as cx\n"
-        "g = torch.Generator(device='cuda').manual_seed(5)\n"
-        "out = []\n"
-        "for M, N, K in [(2048, 8192, 512), (500, 1000, 264)]:\n"
-        "    a = torch.randn(M, K, generator=g, device='cuda').bfloat16()\n"
-        "    b = (torch.randn(K, N, generator=g, device='cuda') * 0.05).bfloat16()\n"
-        "    w = (torch.randn(N, K, generator=g, device='cuda') * 0.05).bfloat16()\n"
-        "    out += [cx.bf16_matmul(a, b).cpu(), cx.linear(a, w).cpu()]\n"
-        "torch.save(out, sys.argv[1])\n")
-    res = {}
-    for flag in ("1", "0"):
-        path = tmp_path / f"out{flag}.pt"
-        env = dict(os.environ, CMPX_TC_TAIL_SPLIT=flag)
-        r = subprocess.run([sys.executable, str(script), str(path)], env=env, capture_output=True, text=True,
-                           timeout=300)
-        assert r.returncode == 0, r.stderr[-2000:]
-        res[flag] = torch.load(path)
-    for x, y in zip(res["1"], res["0"]):
-        assert torch.equal(x, y)

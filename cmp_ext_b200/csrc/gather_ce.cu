@@ -5,12 +5,14 @@
 // The reference has no multi-GPU code; this serves the row-sharded layout
 // of the matmul path: rank r computes rows [r S, (r+1) S) of C and every
 // rank wants the whole C.  The CTA-pair GEMM counts finished output tiles
-// per group of pair-tile columns in device flags (gemm_tc2.cu, col_flags);
-// one copy stream per peer waits on each group's flag with a stream memory
-// operation (cuStreamWaitValue32, GEQ) and then copies that group's columns
-// of this rank's rows into the peer's output with one 2-D cudaMemcpyAsync
-// over NVLink.  Flags are never reset: call e (1, 2, ...) waits for e times
-// a group's per-call count, so back-to-back calls need no clearing launch.
+// per block -- an M group of its raster (group_m pair-tile rows, which it
+// sweeps column by column) times a group of pair-tile columns -- in device
+// flags (gemm_tc2.cu, col_flags).  One copy stream per peer waits on each
+// block's flag with a stream memory operation (cuStreamWaitValue32, GEQ),
+// in the order the GEMM finishes them, and then copies the block into the
+// peer's output with one 2-D cudaMemcpyAsync over NVLink.  Flags are never
+// reset: call e (1, 2, ...) waits for e times a block's per-call count, so
+// back-to-back calls need no clearing launch.
 #include <cstring>
 #include <mutex>
 
@@ -41,7 +43,7 @@ int wait32_fn(WaitValue32Fn* out) {
 using namespace cmpx;
 
 extern "C" int cmpx_gemm_gather_ce(const cmpx_gemm_args* args, void* const* peer_C, int n_peers, int* flags,
-                                   int n_groups, unsigned int epoch, cmpx_stream_t stream,
+                                   int n_flags, int n_groups, unsigned int epoch, cmpx_stream_t stream,
                                    const cmpx_stream_t* copy_streams, int n_copy_streams) {
   if (args == nullptr || n_peers < 0 || n_peers > kMaxPeerOut || flags == nullptr || n_groups < 1 || epoch == 0)
     return CMPX_ERR_INVALID_ARG;
@@ -63,6 +65,9 @@ extern "C" int cmpx_gemm_gather_ce(const cmpx_gemm_args* args, void* const* peer
   const int64_t tiles_n = (args->N + pair_n - 1) / pair_n;
   const int64_t flag_tiles = (tiles_n + n_groups - 1) / n_groups;
   const int64_t groups = (tiles_n + flag_tiles - 1) / flag_tiles;
+  const int64_t group_m = tc2_group_m();
+  const int64_t mgroups = (tiles_m + group_m - 1) / group_m;
+  if (int64_t(n_flags) < mgroups * groups) return CMPX_ERR_WORKSPACE;
   cudaEvent_t ev_start = nullptr;
   if (n_peers > 0) {
     // the copies follow all earlier work on `stream` (e.g. the barrier that
@@ -83,23 +88,30 @@ extern "C" int cmpx_gemm_gather_ce(const cmpx_gemm_args* args, void* const* peer
     if (cudaStreamWaitEvent(copy_streams[c], ev_start, 0) != cudaSuccess) return CMPX_ERR_CUDA;
   cudaEventDestroy(ev_start);
   const char* src = static_cast<const char*>(args->C);
-  for (int64_t j = 0; j < groups; ++j) {
-    const int64_t col0 = j * flag_tiles * pair_n;
-    const int64_t col1 = (j + 1) * flag_tiles * pair_n < args->N ? (j + 1) * flag_tiles * pair_n : args->N;
-    const int64_t ntiles = (col1 - col0 + pair_n - 1) / pair_n;
-    // 8 arrivals per pair tile (4 epilogue warps x 2 CTAs), per call
-    const uint32_t target = uint32_t(uint64_t(epoch) * uint64_t(tiles_m * ntiles * 8));
-    for (int c = 0; c < ns; ++c) {
-      if (wait32(reinterpret_cast<CUstream>(copy_streams[c]), reinterpret_cast<CUdeviceptr>(flags + j), target,
-                 CU_STREAM_WAIT_VALUE_GEQ) != CUDA_SUCCESS)
-        return CMPX_ERR_CUDA;
-    }
-    for (int p = 0; p < n_peers; ++p) {
-      char* dst = static_cast<char*>(peer_C[p]);
-      if (cudaMemcpy2DAsync(dst + col0 * E, size_t(args->ldc * E), src + col0 * E, size_t(args->ldc * E),
-                            size_t((col1 - col0) * E), size_t(args->M), cudaMemcpyDefault,
-                            copy_streams[p % ns]) != cudaSuccess)
-        return CMPX_ERR_CUDA;
+  for (int64_t mg = 0; mg < mgroups; ++mg) {
+    const int64_t row0 = mg * group_m * 256;
+    const int64_t row1 = (mg + 1) * group_m * 256 < args->M ? (mg + 1) * group_m * 256 : args->M;
+    const int64_t mtiles = (row1 - row0 + 255) / 256;
+    for (int64_t j = 0; j < groups; ++j) {
+      const int64_t col0 = j * flag_tiles * pair_n;
+      const int64_t col1 = (j + 1) * flag_tiles * pair_n < args->N ? (j + 1) * flag_tiles * pair_n : args->N;
+      const int64_t ntiles = (col1 - col0 + pair_n - 1) / pair_n;
+      // 8 arrivals per pair tile (4 epilogue warps x 2 CTAs), per call
+      const uint32_t target = uint32_t(uint64_t(epoch) * uint64_t(mtiles * ntiles * 8));
+      int* flag = flags + mg * groups + j;
+      for (int c = 0; c < ns; ++c) {
+        if (wait32(reinterpret_cast<CUstream>(copy_streams[c]), reinterpret_cast<CUdeviceptr>(flag), target,
+                   CU_STREAM_WAIT_VALUE_GEQ) != CUDA_SUCCESS)
+          return CMPX_ERR_CUDA;
+      }
+      for (int p = 0; p < n_peers; ++p) {
+        char* dst = static_cast<char*>(peer_C[p]);
+        const size_t off = size_t(row0 * args->ldc + col0) * E;
+        if (cudaMemcpy2DAsync(dst + off, size_t(args->ldc * E), src + off, size_t(args->ldc * E),
+                              size_t((col1 - col0) * E), size_t(row1 - row0), cudaMemcpyDefault,
+                              copy_streams[p % ns]) != cudaSuccess)
+          return CMPX_ERR_CUDA;
+      }
     }
   }
   // `stream` continues once every copy has landed

@@ -49,8 +49,9 @@ struct Tc2Params {
   int a_bcast;
   int bias_m;
   PeerOut peers;
-  int* col_flags;  // column-progress flags (see Gemm::col_flags), nullptr = none
-  int flag_tiles;
+  int* col_flags;  // progress flags per (M group of the raster, column group), nullptr = none
+  int flag_tiles;     // pair-tile columns per column group
+  int flag_groups_n;  // column groups
   unsigned epi_sleep_ns;  // epilogue's accumulator wait: sleep between polls (0 = spin)
   int* err;
 };
@@ -435,7 +436,7 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
         if (lane == 0) {
           __threadfence_system();
-          atomicAdd(p.col_flags + tn / p.flag_tiles, 1);
+          atomicAdd(p.col_flags + (tm / p.group_m) * p.flag_groups_n + tn / p.flag_tiles, 1);
         }
       }
 
@@ -494,7 +495,7 @@ __global__ void __launch_bounds__(192, 1)
   if (p.col_flags != nullptr && threadIdx.x == 0 && *abort_flag) {
     // A launch that gave up never completes its tiles: release every waiter
     // on the flags (the error word tells the host the output is not valid).
-    const int groups = (p.tiles_n + p.flag_tiles - 1) / p.flag_tiles;
+    const int groups = ((p.tiles_m + p.group_m - 1) / p.group_m) * p.flag_groups_n;
     for (int j = 0; j < groups; ++j) atomicAdd(p.col_flags + j, 1 << 24);
   }
   __syncwarp();
@@ -532,6 +533,7 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   p.peers = g.peers;
   p.col_flags = g.col_flags;
   p.flag_tiles = g.flag_tiles > 0 ? g.flag_tiles : 1;
+  p.flag_groups_n = (p.tiles_n + p.flag_tiles - 1) / p.flag_tiles;
   p.epi_sleep_ns = epilogue_sleep_ns();
   p.err = dev_err;
   const long long total = 1LL * p.tiles_m * p.tiles_n * p.batch;

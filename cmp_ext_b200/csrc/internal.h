@@ -45,10 +45,11 @@ struct Gemm {
   int a_bcast;  // batch > 1 and stride_a == 0: every batch entry uses the same A
   int bias_m;   // bias has M entries (one per row) instead of N (one per column)
   PeerOut peers;  // also write C to these (same layout), n = 0: none
-  // Column-progress flags (CTA-pair kernel only; nullptr = none): after the
-  // output tile in pair-tile column tn is stored, each of the pair's CTAs
-  // adds 1 to col_flags[tn / flag_tiles] (system-scope release), so another
-  // stream can start on finished column groups while the GEMM runs.
+  // Progress flags (CTA-pair kernel only; nullptr = none): after its rows of
+  // the output tile (tm, tn) are stored, each epilogue warp of the pair adds
+  // 1 to col_flags[(tm / group_m) * column_groups + tn / flag_tiles]
+  // (system-scope release; group_m = tc2_group_m(), the raster's M group),
+  // so another stream can start on finished blocks while the GEMM runs.
   int* col_flags = nullptr;
   int flag_tiles = 0;
 };

@@ -341,9 +341,10 @@ void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vecto
 
 // a @ b into `out` (this rank's rows of a row-sharded C) with the rows
 // copied to peer_out[p] on copy_streams[p % n] as tile columns finish
-// (cmpx_gemm_gather_ce).  flags: int32 device tensor of n_groups entries.
+// (cmpx_gemm_gather_ce).  flags: int32 device tensor, at least
+// ceil(ceil(M / 256) / 8) * n_groups entries.
 void matmul_gather_ce(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vector<int64_t> peer_out,
-                      torch::Tensor flags, int64_t epoch, std::vector<int64_t> copy_streams) {
+                      torch::Tensor flags, int64_t n_groups, int64_t epoch, std::vector<int64_t> copy_streams) {
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "matmul_gather_ce: 2-D tensors expected");
   TORCH_CHECK(a.is_cuda() && b.device() == a.device() && out.device() == a.device() && flags.device() == a.device(),
               "matmul_gather_ce: one CUDA device");
@@ -375,7 +376,8 @@ void matmul_gather_ce(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::
   std::vector<cmpx_stream_t> cs(copy_streams.size());
   for (size_t i = 0; i < copy_streams.size(); ++i) cs[i] = reinterpret_cast<cmpx_stream_t>(copy_streams[i]);
   check_status(cmpx_gemm_gather_ce(&args, peers.data(), int(peers.size()), flags.data_ptr<int>(), int(flags.numel()),
-                                   static_cast<unsigned int>(epoch), current_stream(), cs.data(), int(cs.size())),
+                                   int(n_groups), static_cast<unsigned int>(epoch), current_stream(), cs.data(),
+                                   int(cs.size())),
                "matmul_gather_ce");
 }
 
@@ -435,8 +437,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("key"), py::arg("value"), py::arg("scale") = py::none());
   m.def("_matmul_gather_ce", &matmul_gather_ce,
         "a @ b into out with the rows copied to peer outputs on copy streams as tile columns finish (internal)",
-        py::arg("a"), py::arg("b"), py::arg("out"), py::arg("peer_out"), py::arg("flags"), py::arg("epoch"),
-        py::arg("copy_streams"));
+        py::arg("a"), py::arg("b"), py::arg("out"), py::arg("peer_out"), py::arg("flags"), py::arg("n_groups"),
+        py::arg("epoch"), py::arg("copy_streams"));
   m.def("_set_path", &set_path, "force a kernel path for testing: auto, tc, skinny, simt");
   m.def("_matmul_path", &matmul_path, "kernel path cmpx_gemm picks for a packed (M,K)x(K,N) matmul");
   m.def("_version", []() { return std::string(cmpx_version()); });

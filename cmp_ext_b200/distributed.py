@@ -130,7 +130,8 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
 
         st = _CE.get(out.data_ptr())
         if st is None:
-            st = {"flags": torch.zeros(ce_groups, dtype=torch.int32, device=out.device), "epoch": 0,
+            mgroups = ((S + 255) // 256 + 7) // 8  # M groups of 8 pair-tile rows (2048 rows) in this rank's rows
+            st = {"flags": torch.zeros(mgroups * ce_groups, dtype=torch.int32, device=out.device), "epoch": 0,
                   "streams": [torch.cuda.Stream(out.device) for _ in range(max(1, world - 1))]}
             _CE[out.data_ptr()] = st
         st["epoch"] += 1
@@ -138,7 +139,7 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
         offset = rank * S * row_bytes
         peers = [int(h.buffer_ptrs[p]) + offset for p in range(world) if p != rank]
         h.barrier(channel=0)  # every rank is done with the previous contents of its output
-        cx._matmul_gather_ce(a_shard, b, out[rank * S:(rank + 1) * S], peers, st["flags"], st["epoch"],
+        cx._matmul_gather_ce(a_shard, b, out[rank * S:(rank + 1) * S], peers, st["flags"], ce_groups, st["epoch"],
                              [s.cuda_stream for s in st["streams"]])
         h.barrier(channel=0)  # every rank's copies into every output have landed
         return out

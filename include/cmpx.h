@@ -138,20 +138,22 @@ CMPX_API int cmpx_gemm_select_path(const cmpx_gemm_args* args);
  *
  * Computes `args` (fp16/bf16, batch 1, M > 128: the CTA-pair tile kernel)
  * into args->C on `stream`.  The kernel counts finished output tiles per
- * group of 256-column tile columns in `flags` (n_groups ints, zero before
- * the first call); copy_streams[p % n_copy_streams] waits on each group's
- * flag (a stream memory operation, no SM time) and copies that group's
- * columns of the M rows to peer_C[p] (same ldc) with cudaMemcpy2DAsync, i.e.
- * on a copy engine over NVLink, while later tiles are still computing.
- * `stream` waits for every copy before its next work.  `epoch` is 1 on the
- * first call with a given `flags` array and grows by one per call (flags are
- * never cleared).  peer_C entries must be mapped into this process (peer
- * access or a symmetric-memory mapping); the caller orders the peers' use of
- * their outputs (e.g. a barrier before and after).  n_peers = 0 runs the
- * flagged GEMM alone.  CMPX_ERR_UNSUPPORTED when the shape does not run the
- * CTA-pair kernel. */
+ * block -- an M group of its raster (8 pair-tile rows, 2048 rows; the
+ * CMPX_TC_GROUP_M setting) times one of n_groups groups of 256-column tile
+ * columns -- in `flags` (n_flags ints, zero before the first call; at least
+ * ceil(ceil(M / 256) / 8) * n_groups of them, else CMPX_ERR_WORKSPACE).
+ * copy_streams[p % n_copy_streams] waits on each block's flag (a stream
+ * memory operation, no SM time) and copies the block to peer_C[p] (same
+ * ldc) with cudaMemcpy2DAsync, i.e. on a copy engine over NVLink, while later
+ * tiles are still computing.  `stream` waits for every copy before its next
+ * work.  `epoch` is 1 on the first call with a given `flags` array and grows
+ * by one per call (flags are never cleared).  peer_C entries must be mapped
+ * into this process (peer access or a symmetric-memory mapping); the caller
+ * orders the peers' use of their outputs (e.g. a barrier before and after).
+ * n_peers = 0 runs the flagged GEMM alone.  CMPX_ERR_UNSUPPORTED when the
+ * shape does not run the CTA-pair kernel. */
 CMPX_API int cmpx_gemm_gather_ce(const cmpx_gemm_args* args, void* const* peer_C, int n_peers, int* flags,
-                                 int n_groups, unsigned int epoch, cmpx_stream_t stream,
+                                 int n_flags, int n_groups, unsigned int epoch, cmpx_stream_t stream,
                                  const cmpx_stream_t* copy_streams, int n_copy_streams);
 
 /* Replaces launch_add_bias_{fp16,fp32,bf16} (reference

@@ -74,7 +74,7 @@ def lib():
         L.cmpx_version.restype = ctypes.c_char_p
         L.cmpx_gemm_gather_ce.restype = ctypes.c_int
         L.cmpx_gemm_gather_ce.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
-                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint, ctypes.c_void_p,
                                           ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
         _lib = L
     return _lib

@@ -365,20 +365,23 @@ def test_skinny_caller_workspace(cuda, shape):
 
 
 @pytest.mark.parametrize("shape,groups,nstreams", [((512, 2048, 384), 4, 2), ((300, 1000, 136), 3, 1),
-                                                   ((256, 256, 64), 8, 3)],
-                         ids=["even", "ragged", "one-column"])
+                                                   ((256, 256, 64), 8, 3), ((2304, 1024, 128), 2, 3)],
+                         ids=["even", "ragged", "one-column", "two-m-groups"])
 def test_gather_ce_local_peers(cuda, shape, groups, nstreams):
     """cmpx_gemm_gather_ce on one GPU, with local buffers standing in for the
     peers' outputs: every "peer" gets the GEMM's rows through the copy
     streams' flag waits and 2-D copies, on three calls in a row (epochs 1-3;
-    the flags are never cleared)."""
+    the flags are never cleared).  Flags count per (M group of 2048 rows,
+    column group)."""
     M, N, K = shape
     g = torch.Generator(device="cuda").manual_seed(31)
     A = torch.randn(M, K, generator=g, device="cuda").bfloat16()
     B = (torch.randn(K, N, generator=g, device="cuda") * 0.05).bfloat16()
     want = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
     assert cabi.gemm(cabi.gemm_args(A, B, want)) == cabi.OK
-    flags = torch.zeros(groups, dtype=torch.int32, device="cuda")
+    tiles_m, tiles_n = (M + 255) // 256, (N + 255) // 256
+    mgroups = (tiles_m + 7) // 8
+    flags = torch.zeros(mgroups * groups, dtype=torch.int32, device="cuda")
     streams = [torch.cuda.Stream() for _ in range(nstreams)]
     cs = (ctypes.c_void_p * nstreams)(*[s.cuda_stream for s in streams])
     for epoch in (1, 2, 3):
@@ -386,20 +389,29 @@ def test_gather_ce_local_peers(cuda, shape, groups, nstreams):
         peers = [torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(3)]
         pp = (ctypes.c_void_p * 3)(*[p.data_ptr() for p in peers])
         torch.cuda.synchronize()
-        st = cabi.lib().cmpx_gemm_gather_ce(ctypes.byref(cabi.gemm_args(A, B, C)), pp, 3, flags.data_ptr(), groups,
-                                            epoch, torch.cuda.current_stream().cuda_stream, cs, nstreams)
+        st = cabi.lib().cmpx_gemm_gather_ce(ctypes.byref(cabi.gemm_args(A, B, C)), pp, 3, flags.data_ptr(),
+                                            flags.numel(), groups, epoch, torch.cuda.current_stream().cuda_stream,
+                                            cs, nstreams)
         assert st == cabi.OK, cabi.lib().cmpx_status_string(st)
         torch.cuda.current_stream().synchronize()  # the call made this stream wait for the copies
         assert torch.equal(C, want)
         for p in peers:
             assert torch.equal(p, want)
-    tiles_m, tiles_n = (M + 255) // 256, (N + 255) // 256
     ft = (tiles_n + groups - 1) // groups
-    per_group = [min(ft, tiles_n - j * ft) for j in range((tiles_n + ft - 1) // ft)]
-    assert flags[:len(per_group)].tolist() == [3 * tiles_m * t * 8 for t in per_group]
+    ncol = [min(ft, tiles_n - j * ft) for j in range((tiles_n + ft - 1) // ft)]
+    nrow = [min(8, tiles_m - i * 8) for i in range(mgroups)]
+    want_flags = [3 * mt * nt * 8 for mt in nrow for nt in ncol]
+    got_flags = flags.view(mgroups, groups)[:, :len(ncol)].flatten().tolist()
+    assert got_flags == want_flags
     assert cabi.device_error() == 0
+    # a flags array too small for the blocks is refused
+    st = cabi.lib().cmpx_gemm_gather_ce(ctypes.byref(cabi.gemm_args(A, B, C)), pp, 3, flags.data_ptr(),
+                                        mgroups * len(ncol) - 1, groups, 4, torch.cuda.current_stream().cuda_stream,
+                                        cs, nstreams)
+    assert st == cabi.ERR_WORKSPACE
     # shapes that would not run the CTA-pair kernel are refused
     small = torch.empty((64, N), dtype=torch.bfloat16, device="cuda")
     st = cabi.lib().cmpx_gemm_gather_ce(ctypes.byref(cabi.gemm_args(A[:64], B, small)), pp, 3, flags.data_ptr(),
-                                        groups, 4, torch.cuda.current_stream().cuda_stream, cs, nstreams)
+                                        flags.numel(), groups, 4, torch.cuda.current_stream().cuda_stream, cs,
+                                        nstreams)
     assert st == cabi.ERR_UNSUPPORTED

@@ -544,6 +544,41 @@ def attention_record(timer, P, args, device, dtype=torch.float16):
 KIND_NAMES = {torch.float16: "fp16", torch.bfloat16: "bf16", torch.float32: "fp32"}
 
 
+def library_context(timer, P, args, device):
+    """Context only, not this library: the same config-3 GEMM through
+    torch.matmul (cuBLAS) and the attention shape through torch's
+    scaled_dot_product_attention, timed with the same rules, so the kernels
+    here can be read against the vendor libraries on the same GPU and in the
+    same power state."""
+    import torch.nn.functional as F
+
+    out = {}
+    cfg = CONFIGS[3]
+    A, B = make_inputs(cfg, device, seed=0, a_seed=1000)
+    K = max(3, min(args.steps, 20))
+    ms, clocks = timer.run(lambda: torch.matmul(A, B), K, 3)
+    v = cfg.flops / (ms / K / 1e3) / 1e12
+    out["config3_torch_matmul"] = {"value": v, "unit": "TFLOP/s", "ms_per_step": ms / K, "clocks": clocks,
+                                   "tflops_per_mhz": v / clocks["sm_mhz"] if clocks else None}
+    del A, B
+    Bh, H, L, D = 8, 8, 1024, 128
+    g = torch.Generator(device=device).manual_seed(0)
+    sets = [tuple(torch.randn(Bh, H, L, D, generator=g, device=device).half() for _ in range(3)) for _ in range(4)]
+    st = {"i": 0}
+
+    def sdpa():
+        q, k, v_ = sets[st["i"] % 4]
+        st["i"] += 1
+        F.scaled_dot_product_attention(q, k, v_, scale=1.0 / D ** 0.5)
+
+    ms, clocks = timer.run(sdpa, K, 3)
+    v = 4.0 * Bh * H * L * L * D / (ms / K / 1e3) / 1e12
+    out["attention_fp16_torch_sdpa"] = {"value": v, "unit": "TFLOP/s", "ms_per_step": ms / K, "clocks": clocks}
+    sets.clear()
+    torch.cuda.empty_cache()
+    return out
+
+
 def gathered_record(cfg, transport, timer, P, args, device, world, rank):
     """Config 3 M-sharded with the all-gather of C (every rank ends with the
     whole C), and a check of the gathered C: sampled rows of every rank's
@@ -692,6 +727,10 @@ def run_ours(args):
                     sub[f"attention_{KIND_NAMES[dt]}"] = attention_record(timer, P, args, device, dt)
                 except Exception as ex:  # reported, never hidden
                     sub[f"attention_{KIND_NAMES[dt]}"] = {"error": repr(ex)[:300]}
+            try:
+                sub["context_vendor_libraries"] = library_context(timer, P, args, device)
+            except Exception as ex:  # context only
+                sub["context_vendor_libraries"] = {"error": repr(ex)[:300]}
         else:
             c3 = CONFIGS[3]
             if c3.M % world == 0:

@@ -307,30 +307,37 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
         const bool full = kv0 + 128 <= p.S;
         const float sl = p.scale_log2;
         // pass 1: the row maximum over all 128 keys of the block, on the raw
-        // scores (one scaling at the end; the order flips for a negative scale)
-        float mx_hi = -INFINITY, mx_lo = INFINITY;
+        // scores (scaled once at the end; a negative scale needs the minimum,
+        // i.e. the maximum of the negated scores).  Eight independent
+        // partial maxima per chunk keep the dependent-instruction chains
+        // short (a single running maximum is a 128-long serial chain).
+        const float sgn = sl >= 0.0f ? 1.0f : -1.0f;
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t x[32];
           tmem_ld_32x32b_x32(s_addr + c * 32, x);
           tmem_ld_wait();
-          if (full) {
+          if (full && sgn > 0.0f) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              mx_hi = fmaxf(mx_hi, __uint_as_float(x[i]));
-              mx_lo = fminf(mx_lo, __uint_as_float(x[i]));
-            }
+            for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(x[i]));
+          } else if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], -__uint_as_float(x[i]));
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (kv0 + c * 32 + i < p.S) {
-                mx_hi = fmaxf(mx_hi, __uint_as_float(x[i]));
-                mx_lo = fminf(mx_lo, __uint_as_float(x[i]));
-              }
+              if (kv0 + c * 32 + i < p.S) mx8[i & 7] = fmaxf(mx8[i & 7], sgn * __uint_as_float(x[i]));
           }
         }
-        m_new = fmaxf(m_run, sl >= 0.0f ? mx_hi * sl : mx_lo * sl);
-        float sum = 0.0f;
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        m_new = fmaxf(m_run, mx * sgn * sl);
+        float sum8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
         // pass 2: this thread's keys [KPT h, KPT (h + 1)): 64-key chunk
         // (KPT h) / 64 of P, 16-byte units from ((KPT h) % 64) / 8 on
         const int key0 = h * KPT;
@@ -346,13 +353,13 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               pv[i] = ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new));
-              sum += pv[i];
+              sum8[i & 7] += pv[i];
             }
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               pv[i] = (kv0 + key0 + c * 32 + i < p.S) ? ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new)) : 0.0f;
-              sum += pv[i];
+              sum8[i & 7] += pv[i];
             }
           }
           // 16-byte unit u of the row's 128 bytes holds keys [8u, 8u + 8) of the chunk
@@ -367,6 +374,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
             *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = q;
           }
         }
+        const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
         l = l * ex2_approx(m_run - m_new) + sum;
         m_run = m_new;
         tc_fence_before();

@@ -579,7 +579,7 @@ def library_context(timer, P, args, device):
     return out
 
 
-def gathered_record(cfg, transport, timer, P, args, device, world, rank):
+def gathered_record(cfg, transport, timer, P, args, device, world, rank, chunks=1):
     """Config 3 M-sharded with the all-gather of C (every rank ends with the
     whole C), and a check of the gathered C: sampled rows of every rank's
     block against the fp64 product of that rank's A rows, which this rank
@@ -594,7 +594,7 @@ def gathered_record(cfg, transport, timer, P, args, device, world, rank):
         Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
 
     def step():
-        sharded_matmul(A, B, M=cfg.M, gather=True, out=Cfull, transport=transport)
+        sharded_matmul(A, B, M=cfg.M, gather=True, out=Cfull, transport=transport, chunks=chunks)
 
     K = max(3, min(args.steps, 20))
     ms, clocks = timer.run(step, K, 3)
@@ -611,9 +611,10 @@ def gathered_record(cfg, transport, timer, P, args, device, world, rank):
     okt = torch.tensor([1.0 if ok else 0.0], device=device)
     if world > 1:
         dist.all_reduce(okt, op=dist.ReduceOp.MIN)
-    rec = tensor_record(cfg, S, ms / K, clocks, P, kernel_name(cfg, S) + f" + {transport} all-gather")
+    how = f"{transport} all-gather" if chunks == 1 else f"{transport} point-to-point in {chunks} row chunks"
+    rec = tensor_record(cfg, S, ms / K, clocks, P, kernel_name(cfg, S) + f" + {how}")
     job = 2.0 * cfg.M * cfg.N * cfg.K / (ms / K / 1e3) / 1e12
-    rec.update({"job_value": job, "unit": "TFLOP/s", "transport": transport,
+    rec.update({"job_value": job, "unit": "TFLOP/s", "transport": transport, "chunks": chunks,
                 "check": {"all_ranks_ok": bool(okt.item() == 1.0), "max_err_vs_fp64_rows": max(errs),
                           "what": "8 rows of every rank's block of the gathered C on this rank vs fp64"},
                 "bytes_in_per_rank": (world - 1) * S * cfg.N * torch.empty((), dtype=cfg.dtype).element_size()})
@@ -734,11 +735,12 @@ def run_ours(args):
         else:
             c3 = CONFIGS[3]
             if c3.M % world == 0:
-                for tr in ("nccl", "nvlink", "ce"):
+                for tr, ch in (("nccl", 1), ("nccl", 4), ("nvlink", 1), ("ce", 1)):
+                    key = f"gathered_{tr}" + (f"_chunks{ch}" if ch > 1 else "")
                     try:
-                        sub[f"gathered_{tr}"] = gathered_record(c3, tr, timer, P, args, device, world, rank)
+                        sub[key] = gathered_record(c3, tr, timer, P, args, device, world, rank, chunks=ch)
                     except Exception as ex:  # reported, never hidden
-                        sub[f"gathered_{tr}"] = {"error": repr(ex)[:300]}
+                        sub[key] = {"error": repr(ex)[:300]}
             sub["config5_sharded_tf32x3"] = sub_workload(5, timer, P, args, device, world, rank, path="tc",
                                                          sharded=True)
 

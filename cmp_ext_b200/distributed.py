@@ -63,9 +63,9 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
     gather: each rank computes straight into its row block of the full
        output and the blocks are all-gathered in place over NCCL -- no
        staging buffer and no extra copy.
-    chunks: with gather=True, split the shard into this many row chunks and
-       all-gather chunk i (through a staging buffer) while chunk i+1 is
-       multiplied.
+    chunks: with gather=True (NCCL transport), split the shard into this
+       many row chunks; chunk i's rows are sent to every peer (point-to-point,
+       received in place) while chunk i+1 is multiplied.
     op: the per-shard GEMM (defaults to cmp_ext_b200's *_matmul for the dtype;
        tests on CPU pass torch.matmul).
     transport: "nccl" (all-gather after the GEMM), "nvlink" (the GEMM's
@@ -156,24 +156,36 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
             mine.copy_(op(a_shard, b))
         dist.all_gather_into_tensor(out, mine, group=group)  # in place: input is this rank's block of out
         return out
-    # Chunked: all-gather chunk i (into a staging buffer laid out
-    # [chunk][rank][rows]) while the next chunk computes; then scatter rows
-    # into rank-major order.
+    # Chunked: the GEMM runs in row chunks, and as soon as chunk i is queued
+    # its rows go to every peer with point-to-point sends, received straight
+    # into the peers' row blocks of `out` (one NCCL group of sends and
+    # receives per chunk: an all-gather with in-place destinations, no
+    # staging buffer and no reorder copy).  NCCL's stream waits for the
+    # chunk's GEMM; the next chunk's GEMM runs on the compute stream while
+    # the previous chunk is on the wire.
     bounds = [(S * i // chunks, S * (i + 1) // chunks) for i in range(chunks)]
-    parts = [op(a_shard[c0:c1], b) for c0, c1 in bounds[:1]]
-    works, stages = [], []
-    for i, (c0, c1) in enumerate(bounds):
-        stage = torch.empty((world * (c1 - c0), N), dtype=a_shard.dtype, device=a_shard.device)
-        works.append(dist.all_gather_into_tensor(stage, parts[i], group=group, async_op=True))
-        stages.append(stage)
-        if i + 1 < len(bounds):
-            n0, n1 = bounds[i + 1]
-            parts.append(op(a_shard[n0:n1], b))
+    mine = out[rank * S:(rank + 1) * S]
+    works = []
+    for c0, c1 in bounds:
+        if c1 == c0:
+            continue
+        if op_is_default and a_shard.is_cuda:
+            import cmp_ext_b200 as cx
+
+            cx._matmul_into(a_shard[c0:c1], b, mine[c0:c1])
+        else:
+            mine[c0:c1].copy_(op(a_shard[c0:c1], b))
+        ops = []
+        for q in range(world):
+            if q == rank:
+                continue
+            peer = dist.get_global_rank(group, q) if group is not None else q
+            ops.append(dist.P2POp(dist.isend, mine[c0:c1], peer, group))
+            ops.append(dist.P2POp(dist.irecv, out[q * S + c0:q * S + c1], peer, group))
+        if ops:
+            works.extend(dist.batch_isend_irecv(ops))
     for w in works:
         w.wait()
-    for (c0, c1), stage in zip(bounds, stages):
-        stage = stage.view(world, c1 - c0, N)
-        out.view(world, S, N)[:, c0:c1] = stage
     return out
 
 

@@ -588,7 +588,7 @@ def gathered_record(cfg, transport, timer, P, args, device, world, rank, chunks=
 
     S = cfg.M // world
     A, B = make_inputs(cfg, device, seed=0, m=S, a_seed=1000 + rank)
-    if transport in ("nvlink", "ce"):
+    if transport in ("nvlink", "ce", "nvls"):
         Cfull = gather_output(cfg.M, cfg.N, cfg.dtype, device)
     else:
         Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
@@ -658,7 +658,7 @@ def run_ours(args):
     gather = args.gather and world > 1
     if gather:
         from cmp_ext_b200.distributed import gather_output, sharded_matmul
-        if args.transport in ("nvlink", "ce"):
+        if args.transport in ("nvlink", "ce", "nvls"):
             Cfull = gather_output(cfg.M, cfg.N, cfg.dtype, device)
         else:
             Cfull = torch.empty((cfg.M, cfg.N), dtype=cfg.dtype, device=device)
@@ -735,7 +735,7 @@ def run_ours(args):
         else:
             c3 = CONFIGS[3]
             if c3.M % world == 0:
-                for tr, ch in (("nccl", 1), ("nccl", 4), ("nvlink", 1), ("ce", 1)):
+                for tr, ch in (("nccl", 1), ("nccl", 4), ("nvlink", 1), ("ce", 1), ("nvls", 1)):
                     key = f"gathered_{tr}" + (f"_chunks{ch}" if ch > 1 else "")
                     try:
                         sub[key] = gathered_record(c3, tr, timer, P, args, device, world, rank, chunks=ch)
@@ -837,7 +837,7 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="all-gather C to every rank (N>1)")
     ap.add_argument("--chunks", type=int, default=1, help="row chunks for the overlapped gather (1 = in place)")
-    ap.add_argument("--transport", default="nccl", choices=["nccl", "nvlink", "ce"],
+    ap.add_argument("--transport", default="nccl", choices=["nccl", "nvlink", "ce", "nvls"],
                     help="gather: NCCL all-gather, epilogue stores into peers' outputs over NVLink, or copy-engine "
                          "copies of finished tile columns")
     ap.add_argument("--no-e2e", action="store_true")

@@ -178,6 +178,7 @@ int validate(const cmpx_gemm_args* a) {
   }
   if (a->stride_a < 0 || a->stride_b < 0 || a->stride_c < 0) return CMPX_ERR_INVALID_ARG;
   if (a->n_peer_C < 0 || a->n_peer_C > kMaxPeerOut) return CMPX_ERR_INVALID_ARG;
+  if (a->mc_C != nullptr && a->n_peer_C > 0) return CMPX_ERR_INVALID_ARG;
   if (a->n_peer_C > 0) {
     if (a->peer_C == nullptr) return CMPX_ERR_INVALID_ARG;
     for (int i = 0; i < a->n_peer_C; ++i)
@@ -207,6 +208,7 @@ Gemm to_gemm(const cmpx_gemm_args* a) {
   g.a_bcast = (a->batch > 1 && a->stride_a == 0) ? 1 : 0;
   g.bias_m = a->bias_along_m ? 1 : 0;
   g.peers.n = a->n_peer_C;
+  g.mc_C = a->mc_C;
   for (int i = 0; i < kMaxPeerOut; ++i) g.peers.base[i] = i < a->n_peer_C ? a->peer_C[i] : nullptr;
   return g;
 }
@@ -354,6 +356,11 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
   const Gemm g = to_gemm(args);
   const int path = choose_path(g, args->path, &d->info);
   if (path < 0) return CMPX_ERR_UNSUPPORTED;
+  // The multicast output is written by the CTA-pair kernel's epilogue only.
+  if (g.mc_C != nullptr && (g.dtype == CMPX_F32 || path != CMPX_PATH_TC || g.K == 0 ||
+                            tc_pair_n(g, d->info) == 0 || g.N % 8 != 0 || (g.ldc * 2) % 16 != 0 ||
+                            (reinterpret_cast<uintptr_t>(g.mc_C) & 15u) != 0))
+    return CMPX_ERR_UNSUPPORTED;
   if (g.K == 0) return cuda_status(launch_fill_bias(g, s));
   if (path == CMPX_PATH_SIMT) return cuda_status(launch_simt(g, s));
 

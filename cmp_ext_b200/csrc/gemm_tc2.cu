@@ -49,6 +49,7 @@ struct Tc2Params {
   int a_bcast;
   int bias_m;
   PeerOut peers;
+  void* mc_C;  // multicast address of C's layout (nullptr = none), see store_row32_16
   int* col_flags;  // progress flags per (M group of the raster, column group), nullptr = none
   int flag_tiles;     // pair-tile columns per column group
   int flag_groups_n;  // column groups
@@ -144,11 +145,23 @@ __device__ __forceinline__ uint32_t pack2_2(float a, float b, __nv_bfloat16*) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// One 16-byte store through an NVLink multicast address: the switch writes
+// it into every GPU's buffer bound to the multicast object.
+__device__ __forceinline__ void multimem_st16(void* mc_addr, const uint4& q) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+               "f"(__uint_as_float(q.x)), "f"(__uint_as_float(q.y)), "f"(__uint_as_float(q.z)),
+               "f"(__uint_as_float(q.w))
+               : "memory");
+}
+
 // 32 consecutive accumulator columns of one output row -> +bias -> 16-bit
-// output; full 16-byte groups inside [0, N) use vector stores.
+// output; full 16-byte groups inside [0, N) use vector stores.  With `mc`
+// (the multicast address of C's layout; N % 8 == 0) each 16-byte group is
+// written once through it instead of to C and the peer copies.
 template <typename T>
 __device__ __forceinline__ void store_row32_16(T* crow, const T* bias, float rowb, int col0, int N,
-                                               const uint32_t (&r)[32], const PeerOut& po, size_t off) {
+                                               const uint32_t (&r)[32], const PeerOut& po, size_t off,
+                                               void* mc = nullptr) {
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + rowb;
@@ -166,6 +179,10 @@ __device__ __forceinline__ void store_row32_16(T* crow, const T* bias, float row
       q.y = pack2_2(v[g * 8 + 2], v[g * 8 + 3], (T*)nullptr);
       q.z = pack2_2(v[g * 8 + 4], v[g * 8 + 5], (T*)nullptr);
       q.w = pack2_2(v[g * 8 + 6], v[g * 8 + 7], (T*)nullptr);
+      if (mc != nullptr) {
+        multimem_st16(static_cast<T*>(mc) + off + c, q);
+        continue;
+      }
       *reinterpret_cast<uint4*>(crow + c) = q;
       for (int pi = 0; pi < po.n; ++pi) *reinterpret_cast<uint4*>(static_cast<T*>(po.base[pi]) + off + c) = q;
     } else {
@@ -416,7 +433,8 @@ __global__ void __launch_bounds__(192, 1)
             }
             ++chunk_seq;
           } else {
-            if (row < p.M) store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r, p.peers, row_off);
+            if (row < p.M)
+              store_row32_16<OutT>(crow, colb, rowb, tn * PN + c * 32, p.N, r, p.peers, row_off, p.mc_C);
           }
         } else {
           float4* dst = reinterpret_cast<float4*>(part + c * 32);
@@ -480,7 +498,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
               for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(sum[c * 32 + i]);
               if (row < p.M)
-                store_row32_16<OutT>(crow, colb, rowb, tn * PN + h * 128 + c * 32, p.N, r, p.peers, row_off);
+                store_row32_16<OutT>(crow, colb, rowb, tn * PN + h * 128 + c * 32, p.N, r, p.peers, row_off, p.mc_C);
             }
           }
           if (lane == 0) *ctr = 0;
@@ -531,6 +549,7 @@ cudaError_t launch_tc2_run(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   p.a_bcast = g.a_bcast;
   p.bias_m = g.bias_m;
   p.peers = g.peers;
+  p.mc_C = g.mc_C;
   p.col_flags = g.col_flags;
   p.flag_tiles = g.flag_tiles > 0 ? g.flag_tiles : 1;
   p.flag_groups_n = (p.tiles_n + p.flag_tiles - 1) / p.flag_tiles;

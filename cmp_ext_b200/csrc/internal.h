@@ -45,6 +45,10 @@ struct Gemm {
   int a_bcast;  // batch > 1 and stride_a == 0: every batch entry uses the same A
   int bias_m;   // bias has M entries (one per row) instead of N (one per column)
   PeerOut peers;  // also write C to these (same layout), n = 0: none
+  // Multicast address (NVLink multicast object) of C's layout: the CTA-pair
+  // kernel writes every output element once through it, reaching C and every
+  // other buffer bound to the object; nullptr = none.
+  void* mc_C = nullptr;
   // Progress flags (CTA-pair kernel only; nullptr = none): after its rows of
   // the output tile (tm, tn) are stored, each epilogue warp of the pair adds
   // 1 to col_flags[(tm / group_m) * column_groups + tn / flag_tiles]

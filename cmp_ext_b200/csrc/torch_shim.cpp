@@ -305,7 +305,8 @@ torch::Tensor conv2d(torch::Tensor input, torch::Tensor weight, c10::optional<to
 // may be a slice of a larger tensor: row stride out.stride(0), unit column
 // stride).  Used by the M-sharded path to compute straight into its rows of
 // the gathered output.
-void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vector<int64_t> peer_out = {}) {
+void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vector<int64_t> peer_out = {},
+                 int64_t mc_out = 0) {
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "matmul_into: 2-D tensors expected");
   TORCH_CHECK(a.is_cuda() && b.device() == a.device() && out.device() == a.device(), "matmul_into: one CUDA device");
   TORCH_CHECK(a.scalar_type() == b.scalar_type() && out.scalar_type() == a.scalar_type(), "Dtype mismatch");
@@ -336,6 +337,8 @@ void matmul_into(torch::Tensor a, torch::Tensor b, torch::Tensor out, std::vecto
   for (size_t i = 0; i < peer_out.size(); ++i) peers[i] = reinterpret_cast<void*>(peer_out[i]);
   args.peer_C = peers.empty() ? nullptr : peers.data();
   args.n_peer_C = int(peers.size());
+  // mc_out: multicast address (in this process) of `out`'s first element
+  args.mc_C = reinterpret_cast<void*>(mc_out);
   check_status(cmpx_gemm(&args, current_stream()), "matmul_into");
 }
 
@@ -432,7 +435,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bf16_matmul", &bf16_matmul, "a[M,K] @ b[K,N] in bf16 (fp32 accumulate)", py::arg("a"), py::arg("b"));
   m.def("fp32_matmul", &fp32_matmul, "a[M,K] @ b[K,N] in fp32 (3xTF32)", py::arg("a"), py::arg("b"));
   m.def("_matmul_into", &matmul_into, "a @ b written into out (and peer copies of it) (internal)", py::arg("a"),
-        py::arg("b"), py::arg("out"), py::arg("peer_out") = std::vector<int64_t>{});
+        py::arg("b"), py::arg("out"), py::arg("peer_out") = std::vector<int64_t>{}, py::arg("mc_out") = 0);
   m.def("attention", &attention, "scaled dot-product attention (cmpext3.attention)", py::arg("query"),
         py::arg("key"), py::arg("value"), py::arg("scale") = py::none());
   m.def("_matmul_gather_ce", &matmul_gather_ce,

@@ -10,7 +10,6 @@ GEMM of the next chunk on a second stream.
 """
 from __future__ import annotations
 
-import os
 from typing import Callable
 
 import torch
@@ -33,11 +32,10 @@ def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
 
 def gather_output(M: int, N: int, dtype: torch.dtype, device, group=None) -> torch.Tensor:
     """Allocates the full [M, N] output for ``sharded_matmul(..., gather=True,
-    transport="nvlink")``: a symmetric-memory tensor mapped into every rank
-    of `group` (a collective call; every rank passes the same shape).  The
-    buffer is reused by every call that is given it."""
-    # Only peer loads/stores are used, never NVLink multicast objects.
-    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+    transport="nvlink" | "ce" | "nvls")``: a symmetric-memory tensor mapped
+    into every rank of `group` (a collective call; every rank passes the
+    same shape), bound to an NVLink multicast object where the system
+    supports one ("nvls").  The buffer is reused by every call given it."""
     import torch.distributed._symmetric_memory as symm_mem
 
     t = symm_mem.empty((M, N), dtype=dtype, device=device)
@@ -68,7 +66,10 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
        received in place) while chunk i+1 is multiplied.
     op: the per-shard GEMM (defaults to cmp_ext_b200's *_matmul for the dtype;
        tests on CPU pass torch.matmul).
-    transport: "nccl" (all-gather after the GEMM), "nvlink" (the GEMM's
+    transport: "nvls": the GEMM's epilogue writes each output element once
+       through the buffer's NVLink multicast address and the switch delivers
+       it to every rank's output, so each GPU sends its rows once instead of
+       once per peer.  Otherwise "nccl" (all-gather after the GEMM), "nvlink" (the GEMM's
        epilogue stores every output tile to its own rows and, over NVLink, to
        the same rows of every peer's output, overlapping the exchange with the
        remaining tiles) or "ce" (the GEMM counts finished tile columns in
@@ -119,6 +120,22 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
         h.barrier(channel=0)  # every rank is done with the previous contents of its output
         cx._matmul_into(a_shard, b, out[rank * S:(rank + 1) * S], peers)
         h.barrier(channel=0)  # every rank's stores into every output are done
+        return out
+    elif transport == "nvls":
+        h = _SYMM.get(out.data_ptr())
+        if h is None or out.shape != (M, N) or not out.is_contiguous():
+            raise ValueError("transport='nvls' needs the output from gather_output(M, N, ...)")
+        if not op_is_default:
+            raise ValueError("transport='nvls' runs the library's own GEMM (op must be None)")
+        mc = int(h.multicast_ptr) if h.has_multicast_support else 0
+        if mc == 0:
+            raise RuntimeError("transport='nvls': no NVLink multicast support for this buffer")
+        import cmp_ext_b200 as cx
+
+        offset = rank * S * N * out.element_size()
+        h.barrier(channel=0)  # every rank is done with the previous contents of its output
+        cx._matmul_into(a_shard, b, out[rank * S:(rank + 1) * S], [], mc + offset)
+        h.barrier(channel=0)  # every rank's multicast stores have landed everywhere
         return out
     elif transport == "ce":
         h = _SYMM.get(out.data_ptr())

@@ -100,6 +100,12 @@ typedef struct {
                              rows of C in peer GPUs' memory mapped into this process; the epilogue
                              stores every C element to C and to each of them (tile paths only) */
   int n_peer_C;           /* 0..7 */
+  void* mc_C;             /* optional: NVLink multicast address with C's layout (the multicast mapping of
+                             a buffer that C is part of, e.g. symmetric memory bound to a multicast
+                             object on every GPU); the epilogue then stores each output element once,
+                             through it, and the switch writes it into every bound buffer, C's included.
+                             fp16/bf16, M > 128 (the CTA-pair kernel), N % 8 == 0, no peer_C; the
+                             caller orders the other GPUs' use of their buffers. NULL = none */
 } cmpx_gemm_args;
 
 /* Replaces launch_matmul_fp16 (reference src/cuda/fp16_matmul.cu:301-340;

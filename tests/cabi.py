@@ -43,6 +43,7 @@ class GemmArgs(ctypes.Structure):
         ("bias_along_m", ctypes.c_int),
         ("peer_C", ctypes.POINTER(ctypes.c_void_p)),
         ("n_peer_C", ctypes.c_int),
+        ("mc_C", ctypes.c_void_p),
     ]
 
 

@@ -57,6 +57,19 @@ for rep in range(3):  # copy-engine transport: flags are never reset, so repeat 
     assert not torch.isnan(C.float()).any(), "ce gather left rows unwritten"
     err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
     assert err <= 2 ** -7, ("ce", err)
+out3 = gather_output(M, N, torch.bfloat16, "cuda")
+from cmp_ext_b200.distributed import _SYMM
+h3 = _SYMM[out3.data_ptr()]
+if world > 1 and h3.has_multicast_support and int(h3.multicast_ptr) != 0:
+    for rep in range(3):  # epilogue stores through the NVLink multicast address
+        out3.fill_(float("nan"))
+        dist.barrier()
+        C = sharded_matmul(A[r0:r1].contiguous(), B, M=M, gather=True, transport="nvls", out=out3)
+        torch.cuda.synchronize()
+        assert not torch.isnan(C.float()).any(), "nvls gather left rows unwritten"
+        err = ((C.float() - full.float()).abs().max() / full.float().abs().max()).item()
+        assert err <= 2 ** -7, ("nvls", err)
+    print("rank", rank, "nvls checked")
 from cmp_ext_b200.distributed import sharded_host_matmul
 hA = A[r0:r1].cpu().pin_memory()
 hB = B.cpu().pin_memory()

@@ -426,8 +426,23 @@ __global__ void __launch_bounds__(192, 1)
             for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stg + lane * 64 + j * 16) = o[j];
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-              const int row0 = tm * 256 + int(rank) * 128 + q * 32;
+            const int row0 = tm * 256 + int(rank) * 128 + q * 32;
+            if (p.mc_C != nullptr) {
+              // Multicast output: read the staged chunk back so that each
+              // instruction writes 8 rows x 64 contiguous bytes (4 lanes per
+              // row) through the multicast address, instead of 32 scattered
+              // 16-byte pieces.
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int rr = i * 8 + (lane >> 2), piece = lane & 3;
+                const int orow = row0 + rr, ocol = tn * PN + c * 32 + piece * 8;
+                if (orow < p.M && ocol < p.N) {
+                  const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 64 + piece * 16);
+                  multimem_st16(static_cast<OutT*>(p.mc_C) + size_t(b) * p.stride_c + size_t(orow) * p.ldc + ocol, v);
+                }
+              }
+              __syncwarp();  // the buffer is read before it is staged again
+            } else if (lane == 0) {
               for (int d = 0; d < om.n; ++d) tma_store_3d(&om.m[d], stg, tn * PN + c * 32, row0, b);
               bulk_commit();
             }
@@ -593,6 +608,10 @@ cudaError_t launch_tc2_impl(const Gemm& g, const CUtensorMap& tA, const CUtensor
                             const DeviceInfo& dev, int* dev_err, cudaStream_t s, const OutMaps* om) {
   // Peer outputs (staged TMA stores) run whole tiles only.
   if (om != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, true, false>(g, tA, tB, nullptr, dev, dev_err, s, *om);
+  // Multicast output: the staged epilogue with no TMA store maps.
+  static OutMaps none_mc{};
+  if (g.mc_C != nullptr)
+    return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, true, false>(g, tA, tB, nullptr, dev, dev_err, s, none_mc);
   static OutMaps none{};
   if (ws != nullptr) return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, true>(g, tA, tB, ws, dev, dev_err, s, none);
   return launch_tc2_run<FMT, B_KMAJOR, PN, STAGES, false, false>(g, tA, tB, nullptr, dev, dev_err, s, none);

@@ -147,8 +147,10 @@ def sharded_matmul(a_shard: torch.Tensor, b: torch.Tensor, *, M: int | None = No
 
         st = _CE.get(out.data_ptr())
         if st is None:
-            mgroups = ((S + 255) // 256 + 7) // 8  # M groups of 8 pair-tile rows (2048 rows) in this rank's rows
-            st = {"flags": torch.zeros(mgroups * ce_groups, dtype=torch.int32, device=out.device), "epoch": 0,
+            # one flag per (M group, column group); an M group is at least one
+            # 256-row pair tile, whatever the raster's group height
+            nflags = ((S + 255) // 256) * ce_groups
+            st = {"flags": torch.zeros(nflags, dtype=torch.int32, device=out.device), "epoch": 0,
                   "streams": [torch.cuda.Stream(out.device) for _ in range(max(1, world - 1))]}
             _CE[out.data_ptr()] = st
         st["epoch"] += 1

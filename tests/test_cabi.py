@@ -129,3 +129,61 @@ def test_selftest_rejects_bad_limits_without_device():
     f.argtypes = [ctypes.c_ulonglong, ctypes.c_void_p]
     assert f(0, None) == cabi.ERR_INVALID_ARG
     assert f(20_000_000_000, None) == cabi.ERR_INVALID_ARG
+
+
+def _attn_fn():
+    f = cabi.lib().cmpx_attention
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                  ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]
+    return f
+
+
+def test_attention_argument_checks_before_device():
+    f = _attn_fn()
+    p = 0x100000  # fake, 16-byte aligned; never dereferenced
+    assert f(7, p, p, p, p, 1, 1, 8, 64, 1.0, 0, None) == cabi.ERR_INVALID_ARG     # dtype
+    assert f(0, p, p, p, p, -1, 1, 8, 64, 1.0, 0, None) == cabi.ERR_INVALID_ARG    # negative size
+    assert f(0, None, p, p, p, 1, 1, 8, 64, 1.0, 0, None) == cabi.ERR_INVALID_ARG  # null pointer
+    assert f(0, None, None, None, None, 0, 1, 8, 64, 1.0, 0, None) == cabi.OK      # empty: nothing to do
+    assert f(0, None, None, None, None, 1, 1, 0, 64, 1.0, 0, None) == cabi.OK
+
+
+def test_attention_path_selection_is_host_logic():
+    sel = cabi.lib().cmpx_attention_select_path
+    sel.restype = ctypes.c_int
+    sel.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                    ctypes.c_int]
+    p, odd = 0x100000, 0x100008
+    assert sel(cabi.F16, p, p, p, p, 128, cabi.PATH_AUTO) == cabi.PATH_TC
+    assert sel(cabi.BF16, p, p, p, p, 64, cabi.PATH_AUTO) == cabi.PATH_TC
+    assert sel(cabi.F16, p, p, p, p, 80, cabi.PATH_AUTO) == cabi.PATH_SIMT     # D not 64/128
+    assert sel(cabi.F32, p, p, p, p, 128, cabi.PATH_AUTO) == cabi.PATH_SIMT    # fp32: CUDA cores
+    assert sel(cabi.F16, odd, p, p, p, 128, cabi.PATH_AUTO) == cabi.PATH_SIMT  # unaligned: no TMA
+    assert sel(cabi.F32, p, p, p, p, 128, cabi.PATH_TC) == -1
+    assert sel(cabi.F16, p, p, p, p, 1024, cabi.PATH_AUTO) == -1               # beyond the CUDA-core limit
+    assert sel(cabi.F16, p, p, p, p, 128, cabi.PATH_SKINNY) == -1
+
+
+def test_gather_ce_argument_checks_before_device():
+    f = cabi.lib().cmpx_gemm_gather_ce
+    args = _args(M=512)
+    flags = ctypes.c_void_p(0x200000)
+    peers = (ctypes.c_void_p * 1)(0x300000)
+    streams = (ctypes.c_void_p * 1)(None)
+    assert f(None, peers, 1, flags, 4, 4, 1, None, streams, 1) == cabi.ERR_INVALID_ARG       # no args
+    assert f(ctypes.byref(args), peers, 8, flags, 4, 4, 1, None, streams, 1) == cabi.ERR_INVALID_ARG  # > 7 peers
+    assert f(ctypes.byref(args), peers, 1, None, 4, 4, 1, None, streams, 1) == cabi.ERR_INVALID_ARG   # no flags
+    assert f(ctypes.byref(args), peers, 1, flags, 4, 4, 0, None, streams, 1) == cabi.ERR_INVALID_ARG  # epoch 0
+    assert f(ctypes.byref(args), peers, 1, flags, 4, 4, 1, None, None, 0) == cabi.ERR_INVALID_ARG    # no streams
+    a32 = _args(M=512, dtype=cabi.F32)
+    assert f(ctypes.byref(a32), peers, 1, flags, 4, 4, 1, None, streams, 1) == cabi.ERR_UNSUPPORTED  # fp32
+    small = _args(M=64)
+    assert f(ctypes.byref(small), peers, 1, flags, 4, 4, 1, None, streams, 1) == cabi.ERR_UNSUPPORTED  # M <= 128
+
+
+def test_multicast_output_rejected_with_peer_outputs():
+    peers = (ctypes.c_void_p * 1)(0x300000)
+    a = _args(M=512, mc_C=0x400000, n_peer_C=1)
+    a.peer_C = ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p))
+    assert cabi.gemm(a) == cabi.ERR_INVALID_ARG

@@ -107,3 +107,5 @@ def test_sharded_gather(cuda, tmp_path, world):
                        env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
     assert r.stdout.count(" ok") == world
+    if world > 1:  # which transports ran is visible with -rP
+        print("multicast transport checked on", r.stdout.count("nvls checked"), "of", world, "ranks")

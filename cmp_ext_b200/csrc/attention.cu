@@ -315,21 +315,24 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
         float mx8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+        // two halves of 64 scores, each fetched with two loads and one wait
+        // (every wait on tensor memory is a full round trip)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t x[32];
-          tmem_ld_32x32b_x32(s_addr + c * 32, x);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t x[64];
+          tmem_ld_32x32b_x32(s_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+          tmem_ld_32x32b_x32(s_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
           tmem_ld_wait();
           if (full && sgn > 0.0f) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(x[i]));
+            for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(x[i]));
           } else if (full) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], -__uint_as_float(x[i]));
+            for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], -__uint_as_float(x[i]));
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (kv0 + c * 32 + i < p.S) mx8[i & 7] = fmaxf(mx8[i & 7], sgn * __uint_as_float(x[i]));
+            for (int i = 0; i < 64; ++i)
+              if (kv0 + c * 64 + i < p.S) mx8[i & 7] = fmaxf(mx8[i & 7], sgn * __uint_as_float(x[i]));
           }
         }
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
@@ -343,11 +346,14 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
         const int key0 = h * KPT;
         uint8_t* prow = sP + b * Cfg::P_BYTES + (key0 >> 6) * 16384 + r * 128;
         const int u0 = (key0 & 63) >> 3;
+        uint32_t xk[KPT];  // this thread's scores: all loads issued, then one wait
+#pragma unroll
+        for (int c = 0; c < KPT / 32; ++c)
+          tmem_ld_32x32b_x32(s_addr + key0 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&xk[c * 32]));
+        tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < KPT / 32; ++c) {
-          uint32_t x[32];
-          tmem_ld_32x32b_x32(s_addr + key0 + c * 32, x);
-          tmem_ld_wait();
+          const uint32_t* x = &xk[c * 32];
           float pv[32];
           if (full) {
 #pragma unroll
@@ -390,13 +396,16 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
         }
         tc_fence_after();
         const float beta = ex2_approx(m_prev - m_hist);  // 0 while nothing has been folded
+        // this thread's DH columns of O_{j-1}: all loads issued, then one wait
+        {
+          uint32_t x[DH];
 #pragma unroll
-        for (int c = 0; c < DH / 16; ++c) {
-          uint32_t x[16];
-          tmem_ld_32x32b_x16(t_lane + 256u + uint32_t(b * D + h * DH + c * 16), x);
+          for (int c = 0; c < DH / 16; ++c)
+            tmem_ld_32x32b_x16(t_lane + 256u + uint32_t(b * D + h * DH + c * 16),
+                               *reinterpret_cast<uint32_t(*)[16]>(&x[c * 16]));
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[c * 16 + i] = fmaf(o[c * 16 + i], beta, __uint_as_float(x[i]));
+          for (int i = 0; i < DH; ++i) o[i] = fmaf(o[i], beta, __uint_as_float(x[i]));
         }
         tc_fence_before();
         mbar_arrive(&o_empty[b]);

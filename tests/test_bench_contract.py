@@ -54,7 +54,6 @@ def test_rotating_input_sets_exceed_three_l2():
     sets, desc = bench.input_sets(small, "cpu", 64, 0)
     assert len(sets) == 16 and "rotated" in desc  # capped at 16 sets
     assert not torch.equal(sets[0][0], sets[1][0])  # different A per set
-    assert sum(a.numel() * a.element_size() + b.numel() * b.element_size() for a, b in sets) > 0
     one, _ = bench.input_sets(Config(98, "big", torch.float16, 4096, 4096, 4096, "normal", 1.0, "tensor"), "cpu",
                               4096, 0)
     assert len(one) == 4  # 100.7 MB per set: 4 sets exceed 3 x 126 MB

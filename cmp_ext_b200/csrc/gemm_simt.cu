@@ -22,67 +22,100 @@ __device__ __forceinline__ void st_f32(__half* p, float v) { *p = __float2half_r
 __device__ __forceinline__ void st_f32(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 __device__ __forceinline__ void st_f32(float* p, float v) { *p = v; }
 
-constexpr int SB_M = 64, SB_N = 64, SB_K = 16;
+constexpr int SB_M = 128, SB_N = 128, SB_K = 8, SB_PAD = 4;
 
-// 256 threads, each computes a 4x4 block of a 64x64 tile.  blockIdx.z = batch.
+// 256 threads, each computes an 8x8 block of a 128x128 tile: rows
+// {ty*4 .. ty*4+3, 64+ty*4 .. 64+ty*4+3}, columns likewise from tx, so the
+// operands come out of shared memory as float4s with few bank conflicts.
+// K advances 8 at a time through a double-buffered shared-memory tile; the
+// next tile's global loads are held in registers while the current one is
+// multiplied.  Every global access is bounds-checked and uses the caller's
+// strides (any alignment).  blockIdx.z = batch.
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
                                                         T* __restrict__ C, const T* __restrict__ bias, int M, int N,
                                                         int K, long long lda, long long ldb, long long ldc,
                                                         long long sa, long long sb, long long sc, int b_kmajor,
                                                         int bias_m, PeerOut peers) {
-  __shared__ float As[SB_K][SB_M + 4];
-  __shared__ float Bs[SB_K][SB_N + 4];
+  __shared__ __align__(16) float As[2][SB_K][SB_M + SB_PAD];
+  __shared__ __align__(16) float Bs[2][SB_K][SB_N + SB_PAD];
   const int tid = threadIdx.x;
-  const int tx = tid % 16, ty = tid / 16;
+  const int tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * SB_M, n0 = blockIdx.x * SB_N;
   const long long bz = blockIdx.z;
   A += bz * sa;
   B += bz * sb;
   C += bz * sc;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += SB_K) {
-    for (int i = tid; i < SB_M * SB_K; i += 256) {
-      const int r = i / SB_K, k = i % SB_K;
-      const int gm = m0 + r, gk = k0 + k;
-      As[k][r] = (gm < M && gk < K) ? ld_f32(A + gm * lda + gk) : 0.0f;
+  // global -> register staging: 4 A values (row tid/2, k (tid%2)*4 + 0..3)
+  // and 4 B values (B [K,N]: k tid/32, columns (tid%32)*4 + 0..3;
+  // B [N,K]: column tid/2, k (tid%2)*4 + 0..3)
+  float ra[4], rb[4];
+  const int a_r = tid >> 1, a_k = (tid & 1) * 4;
+  auto load = [&](int k0) {
+    const int gm = m0 + a_r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gk = k0 + a_k + i;
+      ra[i] = (gm < M && gk < K) ? ld_f32(A + gm * lda + gk) : 0.0f;
     }
-    for (int i = tid; i < SB_N * SB_K; i += 256) {
-      int c, k;
-      if (b_kmajor) {
-        c = i / SB_K;
-        k = i % SB_K;
-      } else {
-        k = i / SB_N;
-        c = i % SB_N;
+    if (b_kmajor) {
+      const int gn = n0 + a_r;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int gk = k0 + a_k + i;
+        rb[i] = (gn < N && gk < K) ? ld_f32(B + gn * ldb + gk) : 0.0f;
       }
-      const int gn = n0 + c, gk = k0 + k;
-      float v = 0.0f;
-      if (gn < N && gk < K) v = b_kmajor ? ld_f32(B + gn * ldb + gk) : ld_f32(B + gk * ldb + gn);
-      Bs[k][c] = v;
+    } else {
+      const int gk = k0 + (tid >> 5);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int gn = n0 + (tid & 31) * 4 + i;
+        rb[i] = (gn < N && gk < K) ? ld_f32(B + gk * ldb + gn) : 0.0f;
+      }
     }
-    __syncthreads();
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) As[buf][a_k + i][a_r] = ra[i];
+    if (b_kmajor) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Bs[buf][a_k + i][a_r] = rb[i];
+    } else {
+      *reinterpret_cast<float4*>(&Bs[buf][tid >> 5][(tid & 31) * 4]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    }
+  };
+  float acc[8][8] = {};
+  const int nk = (K + SB_K - 1) / SB_K;
+  load(0);
+  store(0);
+  __syncthreads();
+  for (int t = 0; t < nk; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < nk) load((t + 1) * SB_K);  // in flight while this tile is multiplied
 #pragma unroll
     for (int k = 0; k < SB_K; ++k) {
-      float a[4], b[4];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
+      float a[8], bv[8];
+      a[0] = a0.x, a[1] = a0.y, a[2] = a0.z, a[3] = a0.w, a[4] = a1.x, a[5] = a1.y, a[6] = a1.z, a[7] = a1.w;
+      bv[0] = b0.x, bv[1] = b0.y, bv[2] = b0.z, bv[3] = b0.w, bv[4] = b1.x, bv[5] = b1.y, bv[6] = b1.z, bv[7] = b1.w;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[k][ty * 4 + i];
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = Bs[k][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
     }
+    if (t + 1 < nk) store(buf ^ 1);  // the other buffer was last read before the previous barrier
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int gm = m0 + ty * 4 + i;
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
     if (gm >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int gn = n0 + tx * 4 + j;
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
       if (gn >= N) continue;
       float v = acc[i][j];
       if (bias != nullptr) v += ld_f32(bias + (bias_m ? gm : gn));

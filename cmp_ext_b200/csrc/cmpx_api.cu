@@ -462,8 +462,9 @@ int run_gemm(const cmpx_gemm_args* args, cudaStream_t s) {
     if ((st = encode_3d(&tB, op, b_hi, g.N, g.K, g.batch, g.N, sb, 64, 64)) != CMPX_OK) return st;
     if ((st = encode_3d(&tB2, op, b_lo, g.N, g.K, g.batch, g.N, sb, 64, 64)) != CMPX_OK) return st;
   } else {
-    if ((st = encode_3d(&tB, op, b_hi, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
-    if ((st = encode_3d(&tB2, op, b_lo, g.K, g.N, g.batch, g.K, sb, box_k, 128)) != CMPX_OK) return st;
+    const uint32_t box_n = bf ? 128u : uint32_t(tf32x3_block_n());  // rows of B per tile
+    if ((st = encode_3d(&tB, op, b_hi, g.K, g.N, g.batch, g.K, sb, box_k, box_n)) != CMPX_OK) return st;
+    if ((st = encode_3d(&tB2, op, b_lo, g.K, g.N, g.batch, g.K, sb, box_k, box_n)) != CMPX_OK) return st;
   }
   if (bf) return cuda_status(launch_tc_bf16x3(g, tA, tA2, tB, tB2, b_nmajor, d->info, d->err_word, s));
   return cuda_status(launch_tc_tf32x3(g, tA, tA2, tB, tB2, d->info, d->err_word, s));
@@ -532,6 +533,15 @@ unsigned epilogue_sleep_ns() {
     v = x < 0 ? 0 : (x > 100000 ? 100000 : x);
   }
   return unsigned(v);
+}
+
+int tf32x3_block_n() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("CMPX_TF32_BN");
+    v = (e != nullptr && std::strcmp(e, "128") == 0) ? 128 : 256;
+  }
+  return v;
 }
 
 int tc2_group_m() {

@@ -74,7 +74,12 @@ struct TcCfg {
   // first half: two accumulator halves per tile that the epilogue adds.
   static constexpr bool NCAT = FMT == 4;
   static constexpr int ACC_COLS = NCAT ? 2 * BN : BN;
-  static constexpr int NACC = NCAT ? 2 : SPLIT ? 4 : 2;
+  // 3xTF32 with 256-column tiles: two 256-column chunk buffers fill TMEM, and
+  // two groups of four epilogue warps each keep 128 of a row's columns in
+  // registers (one thread per row would need 256 accumulator registers).
+  static constexpr int EPI_GROUPS = (FMT == 2 && BN == 256) ? 2 : 1;
+  static constexpr int THREADS = 64 + 128 * EPI_GROUPS;
+  static constexpr int NACC = NCAT ? 2 : SPLIT ? (EPI_GROUPS == 2 ? 2 : 4) : 2;
   static constexpr int KCH = SPLIT ? 128 / BK : (1 << 30);
   static constexpr uint32_t TMEM_COLS = NACC * ACC_COLS;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 512;
@@ -191,7 +196,7 @@ __device__ __forceinline__ void store_row32(T* crow, const T* bias, float rowb, 
 }
 
 template <int FMT, bool B_KMAJOR, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(TcCfg<FMT, B_KMAJOR, BN, STAGES>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const TcParams p) {
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < Cfg::NACC; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], 128 * Cfg::EPI_GROUPS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -391,9 +396,12 @@ __global__ void __launch_bounds__(192, 1)
       const float rowb = (p.bias_m && bias != nullptr && row < p.M) ? to_f32<OutT>(bias[row]) : 0.0f;
       if constexpr (Cfg::SPLIT) {
         // Sum the tile's chunks in registers (IEEE fp32 adds), then store.
-        float racc[BN];
+        // this thread's share: columns [h * RC, (h + 1) * RC) of the tile
+        constexpr int RC = BN / Cfg::EPI_GROUPS;
+        const int h = Cfg::EPI_GROUPS == 1 ? 0 : (warp - 2) >> 2;
+        float racc[RC];
 #pragma unroll
-        for (int i = 0; i < BN; ++i) racc[i] = 0.0f;
+        for (int i = 0; i < RC; ++i) racc[i] = 0.0f;
         for (int kc = 0; kc < num_kb; kc += Cfg::KCH, ++cc) {
           const int acc = int(cc % Cfg::NACC);
           const uint32_t acc_phase = (cc / Cfg::NACC) & 1;
@@ -405,13 +413,18 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * Cfg::ACC_COLS);
 #pragma unroll
-          for (int c = 0; c < Cfg::ACC_COLS / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(t_row + c * 32, r);
-            tmem_ld_wait();
-            const int o = (c * 32) % BN;  // FMT 4: the second half adds onto the same columns
+          for (int cc2 = 0; cc2 < Cfg::ACC_COLS / 32 / Cfg::EPI_GROUPS; ++cc2) {
+            const int c = h * (RC / 32) + cc2;
+            const int o = (c * 32) % BN - h * RC;  // FMT 4: the second half adds onto the same columns
 #pragma unroll
-            for (int i = 0; i < 32; ++i) racc[o + i] = __fadd_rn(racc[o + i], __uint_as_float(r[i]));
+            for (int hh = 0; hh < 2; ++hh) {  // 16 columns at a time keeps the register count down
+              uint32_t r[16];
+              tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                racc[o + hh * 16 + i] = __fadd_rn(racc[o + hh * 16 + i], __uint_as_float(r[i]));
+            }
           }
           tc_fence_before();
           mbar_arrive(&acc_empty[acc]);
@@ -419,11 +432,11 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) break;
         if (row < p.M) {
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = 0; c < RC / 32; ++c) {
             uint32_t r[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(racc[c * 32 + i]);
-            store_row32<OutT>(crow, colb, rowb, tn * BN + c * 32, p.N, r, p.peers, row_off);
+            store_row32<OutT>(crow, colb, rowb, tn * BN + h * RC + c * 32, p.N, r, p.peers, row_off);
           }
         }
       } else {
@@ -489,7 +502,7 @@ cudaError_t launch_tc_impl(const Gemm& g, const CUtensorMap& tA, const CUtensorM
   const int grid = int(total < dev.num_sms ? total : dev.num_sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -512,6 +525,7 @@ cudaError_t launch_tc_f16(const Gemm& g, const CUtensorMap& tA, const CUtensorMa
 
 cudaError_t launch_tc_tf32x3(const Gemm& g, const CUtensorMap& tA, const CUtensorMap& tA2, const CUtensorMap& tB,
                              const CUtensorMap& tB2, const DeviceInfo& dev, int* dev_err, cudaStream_t s) {
+  if (tf32x3_block_n() == 256) return launch_tc_impl<2, true, 256, 2>(g, tA, tB, tA2, tB2, dev, dev_err, s);
   return launch_tc_impl<2, true, 128, 3>(g, tA, tB, tA2, tB2, dev, dev_err, s);
 }
 

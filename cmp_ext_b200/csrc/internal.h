@@ -150,6 +150,9 @@ unsigned epilogue_sleep_ns();
 // Pair tiles per M group of the CTA-pair kernel's raster (CMPX_TC_GROUP_M,
 // default 8): the tiles of one group share A rows and walk B's columns.
 int tc2_group_m();
+// Tile width of the 3xTF32 kernel: 256 (128 x 256 tiles, two stages) unless
+// CMPX_TF32_BN=128 (128 x 128 tiles, three stages).
+int tf32x3_block_n();
 // Fills `attr` (one slot) and cfg.attrs / cfg.numAttrs for a PDL launch, or
 // leaves cfg without attributes when PDL is off.
 inline void apply_pdl(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int used) {

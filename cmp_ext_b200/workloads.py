@@ -2,7 +2,7 @@
 synthetic inputs (no dataset is involved: the reference benchmarks random
 matrices, tools/bench.py:156-193).
 
-Config ids follow the order of the configs list the path is judged on:
+Config ids follow the order of the benchmark configs of the matmul path:
   1  fp32 257 x 383 x 511,  A,B ~ N(0,1)                     (odd shape)
   2  fp16 4096^3,           A,B ~ U(-1,1)                     (tensor-bound)
   3  bf16 M=16384 K=8192 N=8192, A ~ N(0,1), B ~ N(0,0.02)    (prefill, M-sharded)

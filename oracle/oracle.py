@@ -6,7 +6,7 @@
 * ``ref_gpu_matmul``  -- the reference's own kernels compiled from its sources
   into oracle/_ref/libref_matmul.so (GPU only).
 * ``fp64_matmul`` and ``normwise_err`` -- the ground truth and the error
-  metric both sides are judged by: max|C - C64| / max|C64|.
+  metric both sides are measured with: max|C - C64| / max|C64|.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may use
 this module; the product never does.

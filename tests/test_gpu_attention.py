@@ -104,15 +104,21 @@ def test_simt_attention(cuda, dtype, D, S):
         assert err <= ref_err + TOL[dtype], (err, ref_err)
 
 
-def test_attention_large_logits(cuda):
-    """Scores far from zero (running maximum moves by hundreds between
-    blocks): the online softmax must rescale, never overflow."""
-    q, k, v = _inputs(1, 2, 640, 128, torch.float16, seed=5)
-    k = k * torch.linspace(0.1, 8.0, 640, device="cuda", dtype=torch.float16)[None, None, :, None]
-    scale = 1.0
+@pytest.mark.parametrize("dtype,D,top,scale", [
+    (torch.float16, 128, 8.0, 1.0),     # the maximum moves by hundreds between blocks
+    (torch.bfloat16, 64, 8.0, -1.0),    # negative scale: the row minimum leads
+    (torch.float16, 64, 1.5, 1.0),      # the maximum creeps up by less than the rescale step
+    (torch.bfloat16, 128, 1.5, 0.5),
+])
+def test_attention_large_logits(cuda, dtype, D, top, scale):
+    """Scores far from zero whose running maximum grows block after block:
+    the online softmax must rescale (or keep P within range while it does
+    not), never overflow."""
+    q, k, v = _inputs(1, 2, 640, D, dtype, seed=5)
+    k = k * torch.linspace(0.1, top, 640, device="cuda", dtype=dtype)[None, None, :, None]
     out = _run(q, k, v, scale, cabi.PATH_TC)
     err, _ = _err(out, q, k, v, scale)
-    assert err <= BOUND[torch.float16], err
+    assert err <= BOUND[dtype], err
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])

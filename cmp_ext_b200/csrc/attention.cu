@@ -81,6 +81,36 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Blackwell's paired fp32 arithmetic: two lanes in one 64-bit register, one
+// instruction, each lane rounded exactly as the scalar fmaf / + (.rn), so a
+// softmax written with them gives the same bits as the scalar one with about
+// half the issue slots.  max3f is the three-input maximum (exact).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2unpack(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -90,7 +120,9 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int FMT, int D, int TPR>
+// PK = 1: the softmax uses the paired / three-input instructions above (same
+// results bit for bit); PK = 0: scalar instructions only.
+template <int FMT, int D, int TPR, int PK>
 __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -323,7 +355,15 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
           tmem_ld_32x32b_x32(s_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
           tmem_ld_32x32b_x32(s_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
           tmem_ld_wait();
-          if (full && sgn > 0.0f) {
+          if (PK && full && sgn > 0.0f) {
+#pragma unroll
+            for (int i = 0; i < 64; i += 2)
+              mx8[(i >> 1) & 7] = max3f(mx8[(i >> 1) & 7], __uint_as_float(x[i]), __uint_as_float(x[i + 1]));
+          } else if (PK && full) {
+#pragma unroll
+            for (int i = 0; i < 64; i += 2)
+              mx8[(i >> 1) & 7] = max3f(mx8[(i >> 1) & 7], -__uint_as_float(x[i]), -__uint_as_float(x[i + 1]));
+          } else if (full && sgn > 0.0f) {
 #pragma unroll
             for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(x[i]));
           } else if (full) {
@@ -355,7 +395,27 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
         for (int c = 0; c < KPT / 32; ++c) {
           const uint32_t* x = &xk[c * 32];
           float pv[32];
-          if (full) {
+          if (PK && full) {
+            // lanes (i, i + 1) of pair (i & 7) / 2 are sum8[i & 7] and
+            // sum8[(i & 7) + 1]: the scalar loop's association exactly
+            const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-m_new, -m_new);
+            uint64_t s2[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) s2[k] = f2pack(sum8[2 * k], sum8[2 * k + 1]);
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float2 t = f2unpack(fma2(f2pack(__uint_as_float(x[i]), __uint_as_float(x[i + 1])), sl2, nm2));
+              pv[i] = ex2_approx(t.x);
+              pv[i + 1] = ex2_approx(t.y);
+              s2[(i & 7) >> 1] = add2(s2[(i & 7) >> 1], f2pack(pv[i], pv[i + 1]));
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 t = f2unpack(s2[k]);
+              sum8[2 * k] = t.x;
+              sum8[2 * k + 1] = t.y;
+            }
+          } else if (full) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               pv[i] = ex2_approx(fmaf(__uint_as_float(x[i]), sl, -m_new));
@@ -405,7 +465,19 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
                                *reinterpret_cast<uint32_t(*)[16]>(&x[c * 16]));
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < DH; ++i) o[i] = fmaf(o[i], beta, __uint_as_float(x[i]));
+          if (PK) {
+            const uint64_t b2 = f2pack(beta, beta);
+#pragma unroll
+            for (int i = 0; i < DH; i += 2) {
+              const float2 t = f2unpack(
+                  fma2(f2pack(o[i], o[i + 1]), b2, f2pack(__uint_as_float(x[i]), __uint_as_float(x[i + 1]))));
+              o[i] = t.x;
+              o[i + 1] = t.y;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < DH; ++i) o[i] = fmaf(o[i], beta, __uint_as_float(x[i]));
+          }
         }
         tc_fence_before();
         mbar_arrive(&o_empty[b]);
@@ -518,11 +590,11 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const T* __restrict
   }
 }
 
-template <int FMT, int D, int TPR>
+template <int FMT, int D, int TPR, int PK>
 cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int64_t BH, int64_t S, float scale,
                       int* err, cudaStream_t s) {
   using Cfg = AttnCfg<D, TPR>;
-  auto kern = attention_tc_kernel<FMT, D, TPR>;
+  auto kern = attention_tc_kernel<FMT, D, TPR, PK>;
   static_assert(Cfg::SMEM <= 232448, "shared memory budget");
   static unsigned long long smem_set = 0;
   cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
@@ -575,6 +647,18 @@ int attention_threads_per_row() {
   return v;
 }
 
+// The softmax of the two-threads-per-row kernel in paired fp32 / three-input
+// max instructions (default), or in scalar ones with CMPX_ATTN_PACKED=0; the
+// results are the same bit for bit.
+bool attention_packed() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("CMPX_ATTN_PACKED");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 }  // namespace
 
 int attention_path(int dtype, const void* Q, const void* K, const void* V, const void* O, int64_t D, int requested) {
@@ -609,20 +693,25 @@ extern "C" int cmpx_attention(int dtype, const void* Q, const void* K, const voi
   if (pth == CMPX_PATH_TC) {
     if (BH * ((S + 127) / 128) > 0x7fffffffLL) return CMPX_ERR_UNSUPPORTED;
     const bool four = attention_threads_per_row() == 4;
+    const bool packed = attention_packed();
     if (dtype == CMPX_F16) {
       if (D == 64)
-        e = four ? launch_tc<0, 64, 4>(Q, K, V, O, BH, S, scale, err, stream)
-                 : launch_tc<0, 64, 2>(Q, K, V, O, BH, S, scale, err, stream);
+        e = four ? launch_tc<0, 64, 4, 0>(Q, K, V, O, BH, S, scale, err, stream)
+             : packed ? launch_tc<0, 64, 2, 1>(Q, K, V, O, BH, S, scale, err, stream)
+                      : launch_tc<0, 64, 2, 0>(Q, K, V, O, BH, S, scale, err, stream);
       else
-        e = four ? launch_tc<0, 128, 4>(Q, K, V, O, BH, S, scale, err, stream)
-                 : launch_tc<0, 128, 2>(Q, K, V, O, BH, S, scale, err, stream);
+        e = four ? launch_tc<0, 128, 4, 0>(Q, K, V, O, BH, S, scale, err, stream)
+             : packed ? launch_tc<0, 128, 2, 1>(Q, K, V, O, BH, S, scale, err, stream)
+                      : launch_tc<0, 128, 2, 0>(Q, K, V, O, BH, S, scale, err, stream);
     } else {
       if (D == 64)
-        e = four ? launch_tc<1, 64, 4>(Q, K, V, O, BH, S, scale, err, stream)
-                 : launch_tc<1, 64, 2>(Q, K, V, O, BH, S, scale, err, stream);
+        e = four ? launch_tc<1, 64, 4, 0>(Q, K, V, O, BH, S, scale, err, stream)
+             : packed ? launch_tc<1, 64, 2, 1>(Q, K, V, O, BH, S, scale, err, stream)
+                      : launch_tc<1, 64, 2, 0>(Q, K, V, O, BH, S, scale, err, stream);
       else
-        e = four ? launch_tc<1, 128, 4>(Q, K, V, O, BH, S, scale, err, stream)
-                 : launch_tc<1, 128, 2>(Q, K, V, O, BH, S, scale, err, stream);
+        e = four ? launch_tc<1, 128, 4, 0>(Q, K, V, O, BH, S, scale, err, stream)
+             : packed ? launch_tc<1, 128, 2, 1>(Q, K, V, O, BH, S, scale, err, stream)
+                      : launch_tc<1, 128, 2, 0>(Q, K, V, O, BH, S, scale, err, stream);
     }
   } else {
     if ((BH * S + 3) / 4 > 0x7fffffffLL) return CMPX_ERR_UNSUPPORTED;

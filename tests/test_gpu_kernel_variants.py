@@ -42,3 +42,35 @@ def test_bf16x3_three_mma_variant(cuda):
                         os.path.join(HERE, "test_gpu_parity.py"), "-k", "bf16x3"],
                        env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+_ATTN_CHILD = r"""
+import sys, torch
+import cmp_ext_b200 as cx
+outs = []
+for dt in (torch.float16, torch.bfloat16):
+    for (B, H, S, D, scale) in ((2, 3, 1024, 128, None), (1, 2, 333, 64, None), (1, 1, 257, 128, -0.2),
+                                (1, 1, 640, 64, 3.0)):
+        g = torch.Generator(device="cuda").manual_seed(S + D)
+        q, k, v = (torch.randn(B, H, S, D, generator=g, device="cuda").to(dt) for _ in range(3))
+        outs.append(cx.attention(q, k, v, scale=scale).cpu())
+torch.save(outs, sys.argv[1])
+"""
+
+
+def test_attention_packed_softmax_bit_identical(cuda, tmp_path):
+    """The tensor-core attention softmax in paired fp32 / three-input max
+    instructions (default) gives the same bits as its scalar form
+    (CMPX_ATTN_PACKED=0): fp16 and bf16, D 64 and 128, ragged S, negative
+    and large scales."""
+    import torch
+    res = {}
+    for pk in ("1", "0"):
+        f = tmp_path / f"attn{pk}.pt"
+        env = dict(os.environ, CMPX_ATTN_PACKED=pk, PYTHONPATH=os.path.dirname(HERE))
+        r = subprocess.run([sys.executable, "-c", _ATTN_CHILD, str(f)], env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        res[pk] = torch.load(f)
+    for a, b in zip(res["1"], res["0"]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))

@@ -529,7 +529,8 @@ def attention_record(timer, P, args, device, dtype=torch.float16):
     ach = fl / (ms / K / 1e3) / 1e12
     peak, kind = pick_peak(P, clocks)
     rec = {"workload": f"attention {B}x{H}x{L}x{D} {KIND_NAMES[dtype]} (reference tools/bench.py shape)",
-           "kernel": "attention_tc_kernel", "value": ach, "unit": "TFLOP/s", "ms_per_step": ms / K, "steps": K,
+           "kernel": ("attention_tc_kernel" if os.environ.get("CMPX_ATTN_KERNEL", "").startswith("o")
+                      else "attention_pp_kernel"), "value": ach, "unit": "TFLOP/s", "ms_per_step": ms / K, "steps": K,
            "clocks": clocks, "err_vs_fp64_rows": err, "l2": "4 resident input sets rotated per step",
            "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "peak_kind": kind, "frac": ach / peak,
                         "unit": "TFLOP/s", "flops_per_step": fl},

@@ -5,8 +5,11 @@
 //  src/cuda/fp32_attention.cu:35 attention_fp32_strict_kernel;
 //  launchers declared at src/main.cpp:48-50, wrapper src/main.cpp:1027-1098).
 //
-// fp16 / bf16 with D = 64 or 128: a tcgen05 flash-attention kernel.  One CTA
-// owns 128 query rows of one (batch, head):
+// fp16 / bf16 with D = 64 or 128: tcgen05 flash-attention kernels.  The
+// default, attention_pp_kernel (further down), gives each CTA two 128-row
+// query tiles so one tile's products run while the other is in softmax.
+// The one-tile kernel, attention_tc_kernel: one CTA owns 128 query rows of
+// one (batch, head):
 //   * warp 0 (TMA): Q once, then K_j and V_j blocks of 128 keys into two
 //     separate double-buffered rings (a K slot frees after its QK^T MMA, a V
 //     slot after its PV MMA, so the next K block streams in early);
@@ -103,6 +106,11 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ float max3f(float a, float b, float c) {
@@ -464,7 +472,6 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
             tmem_ld_32x32b_x16(t_lane + 256u + uint32_t(b * D + h * DH + c * 16),
                                *reinterpret_cast<uint32_t(*)[16]>(&x[c * 16]));
           tmem_ld_wait();
-#pragma unroll
           if (PK) {
             const uint64_t b2 = f2pack(beta, beta);
 #pragma unroll
@@ -508,6 +515,354 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
         q.z = pack2(o[g * 8 + 4] * inv, o[g * 8 + 5] * inv, (T*)nullptr);
         q.w = pack2(o[g * 8 + 6] * inv, o[g * 8 + 7] * inv, (T*)nullptr);
         reinterpret_cast<uint4*>(orow)[g] = q;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------- two query tiles per CTA
+// attention_pp_kernel: one CTA owns 256 query rows (tiles A and B) of one
+// (batch, head), so the tensor core works on one tile's products while the
+// other tile is in softmax:
+//   * warp 0 (TMA): both Q tiles once, then K_0, V_0, K_1, V_1, ... through
+//     one shared ring of NS slots;
+//   * warp 1 (one thread): S_t = Q_t K_j^T into tile t's 128-column TMEM
+//     buffer as soon as tile t's softmax has read the previous S_t out, and
+//     O_t += P_t V_j into tile t's D-column accumulator once P_t is written;
+//   * warps 2-5 (tile A) and 6-9 (tile B): one thread per query row, holding
+//     the row's 128 scores of a block in registers: the running maximum and
+//     sum in fp32, P = exp2(s * scale * log2 e - m) as 16-bit values into
+//     shared memory (128-byte-swizzled K-major), and, when a row's maximum
+//     grew, O_t in tensor memory scaled by exp2(m_old - m_new) before the
+//     next P_t V_j accumulates into it (the factor is exactly 1 when the
+//     maximum did not move, so skipping that case changes nothing).  At the
+//     end O_t / l is rounded once.
+template <int D>
+struct PPCfg {
+  static constexpr int THREADS = 64 + 256;         // TMA warp, MMA warp, 2 x 4 softmax warps
+  static constexpr int QCH = D / 64;
+  static constexpr int TILE_BYTES = 128 * D * 2;
+  static constexpr int P_BYTES = 128 * 128 * 2;
+  static constexpr int NS = D == 128 ? 3 : 6;      // K/V ring slots
+  static constexpr size_t SMEM = size_t(TILE_BYTES) * (2 + NS) + 2 * P_BYTES + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = 512;       // S_A S_B (128 each), O_A O_B (D each)
+  static_assert(D == 64 || D == 128, "tensor-core attention supports D = 64 or 128");
+};
+
+template <int FMT, int D>
+__global__ void __launch_bounds__(PPCfg<D>::THREADS, 1)
+    attention_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using Cfg = PPCfg<D>;
+  using T = typename std::conditional<FMT == 0, __half, __nv_bfloat16>::type;
+  constexpr int NS = Cfg::NS;
+  constexpr uint32_t IDESC_QK = make_idesc(uint32_t(FMT), 0u, 0u, 128, 128);
+  constexpr uint32_t IDESC_PV = make_idesc(uint32_t(FMT), 0u, 1u, 128, D);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+  uint8_t* sQ = smem;                                  // [2] tiles
+  uint8_t* sKV = sQ + 2 * Cfg::TILE_BYTES;             // [NS] slots
+  uint8_t* sP = sKV + NS * Cfg::TILE_BYTES;            // [2] tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = q_full + 1;        // [NS]
+  uint64_t* kv_empty = kv_full + NS;     // [NS]
+  uint64_t* s_full = kv_empty + NS;      // [2] S_t computed
+  uint64_t* s_free = s_full + 2;         // [2] S_t read out by tile t's softmax
+  uint64_t* p_full = s_free + 2;         // [2] P_t written and O_t rescaled
+  uint64_t* o_full = p_full + 2;         // [2] P_t V_j accumulated into O_t
+  uint64_t* drain = o_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x / p.qtiles;                 // qtiles = CTAs per (batch, head) here
+  const int q0 = (blockIdx.x - bh * p.qtiles) * 256;
+  const int nt = q0 + 128 < p.S ? 2 : 1;                // query tiles of this CTA
+  const int nkv = (p.S + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, uint32_t(nt * Cfg::TILE_BYTES));
+      for (int t = 0; t < nt; ++t)
+#pragma unroll
+        for (int c = 0; c < Cfg::QCH; ++c)
+          tma_load_3d(sQ + t * Cfg::TILE_BYTES + c * 16384, &tmQ, q_full, c * 64, q0 + t * 128, bh);
+      // items 2j (K_j) and 2j + 1 (V_j) through the ring
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < 2 * nkv; ++i) {
+        const int slot = i % NS;
+        if (!mbar_wait(&kv_empty[slot], ((i / NS) & 1) ^ 1, abort_flag)) {
+          rec_err(p.err, abort_flag, kDevTimeoutEmpty);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[slot], Cfg::TILE_BYTES);
+        const CUtensorMap* m = (i & 1) ? &tmV : &tmK;
+#pragma unroll
+        for (int c = 0; c < Cfg::QCH; ++c)
+          tma_load_3d(sKV + slot * Cfg::TILE_BYTES + c * 16384, m, &kv_full[slot], c * 64, (i >> 1) * 128, bh);
+        ++issued;
+      }
+      if (!ok) {
+        // let the copies in flight land before the CTA exits (bounded waits)
+        volatile int never = 0;
+        mbar_wait(q_full, 0, &never);
+        for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
+          mbar_wait(&kv_full[i % NS], (i / NS) & 1, &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      if (!ok) rec_err(p.err, abort_flag, kDevTimeoutFull);
+      auto kv_wait = [&](int i) -> bool {
+        if (mbar_wait(&kv_full[i % NS], (i / NS) & 1, abort_flag)) return true;
+        rec_err(p.err, abort_flag, kDevTimeoutFull);
+        return false;
+      };
+      auto wait_or_fail = [&](uint64_t* bar, int parity, int code) -> bool {
+        if (mbar_wait(bar, uint32_t(parity), abort_flag)) return true;
+        rec_err(p.err, abort_flag, code);
+        return false;
+      };
+      auto qk = [&](int t, int j) {
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + t * Cfg::TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sKV + ((2 * j) % NS) * Cfg::TILE_BYTES);
+        const uint32_t d_tmem = tmem_base + uint32_t(t * 128);
+#pragma unroll
+        for (int c = 0; c < Cfg::QCH; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(d_tmem, make_sdesc_sw128(q_addr + c * 16384 + kk * 32, 16, 1024),
+                    make_sdesc_sw128(k_addr + c * 16384 + kk * 32, 16, 1024), IDESC_QK, (c | kk) != 0 ? 1u : 0u);
+        mma_commit(&s_full[t]);
+      };
+      auto pv = [&](int t, int j) {
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + t * Cfg::P_BYTES);
+        const uint32_t v_addr = smem_u32(sKV + ((2 * j + 1) % NS) * Cfg::TILE_BYTES);
+        const uint32_t d_tmem = tmem_base + 256u + uint32_t(t * D);
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(d_tmem, make_sdesc_sw128(p_addr + c2 * 16384 + kk * 32, 16, 1024),
+                    make_sdesc_sw128(v_addr + (c2 * 64 + kk * 16) * 128, 16384, 1024), IDESC_PV,
+                    (j | c2 | kk) != 0 ? 1u : 0u);
+        mma_commit(&o_full[t]);
+      };
+      if (ok) ok = kv_wait(0);
+      if (ok) {
+        for (int t = 0; t < nt; ++t) qk(t, 0);
+        mma_commit(&kv_empty[0]);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const bool more = j + 1 < nkv;
+        if (more) ok = kv_wait(2 * j + 2);
+        for (int t = 0; ok && t < nt; ++t) {
+          if (more) {
+            ok = wait_or_fail(&s_free[t], j & 1, kDevTimeoutAccEmpty);
+            if (!ok) break;
+            qk(t, j + 1);
+          }
+          ok = wait_or_fail(&p_full[t], j & 1, kDevTimeoutFull);
+          if (ok && t == 0) ok = kv_wait(2 * j + 1);
+          if (ok) pv(t, j);
+        }
+        if (ok) {
+          if (more) mma_commit(&kv_empty[(2 * j + 2) % NS]);
+          mma_commit(&kv_empty[(2 * j + 1) % NS]);
+        }
+      }
+      if (!ok) {
+        mma_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never);
+      }
+    }
+  } else if ((warp - 2) >> 2 < nt) {
+    // ------------------------------------------------------------ softmax + output (warps 2..9)
+    const int t = (warp - 2) >> 2;   // query tile
+    const int qw = warp & 3;         // TMEM lane quarter this warp may access
+    const int r = qw * 32 + lane;    // row of the tile
+    const uint32_t t_lane = tmem_base + (uint32_t(qw * 32) << 16);
+    const uint32_t s_col = uint32_t(t * 128), o_col = 256u + uint32_t(t * D);
+    const float sl = p.scale_log2;
+    const float sgn = sl >= 0.0f ? 1.0f : -1.0f;
+    uint8_t* prow = sP + t * Cfg::P_BYTES + r * 128;
+    float m_run = -INFINITY, l = 0.0f;
+    bool ok = true;
+#pragma unroll 1
+    for (int j = 0; j < nkv; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t x[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tmem_ld_32x32b_x32(t_lane + s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&x[c * 32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);   // S_t may be overwritten by the next block's QK
+      const int kv0 = j * 128;
+      const bool full = kv0 + 128 <= p.S;
+      // the row maximum on the raw scores (of the negated ones for a negative
+      // scale), eight independent partial maxima
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+      if (full && sgn > 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 128; i += 2)
+          mx8[(i >> 1) & 7] = max3f(mx8[(i >> 1) & 7], __uint_as_float(x[i]), __uint_as_float(x[i + 1]));
+      } else if (full) {
+#pragma unroll
+        for (int i = 0; i < 128; i += 2)
+          mx8[(i >> 1) & 7] = max3f(mx8[(i >> 1) & 7], -__uint_as_float(x[i]), -__uint_as_float(x[i + 1]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (kv0 + i < p.S) mx8[i & 7] = fmaxf(mx8[i & 7], sgn * __uint_as_float(x[i]));
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_new = fmaxf(m_run, mx * sgn * sl);
+      const float alpha = ex2_approx(m_run - m_new);   // 0 for the first block, 1 when m did not move
+      // P = exp2(s * sl - m_new) in place of the scores, with the row sum
+      uint64_t s2[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) s2[k] = f2pack(0.0f, 0.0f);
+      const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-m_new, -m_new);
+#pragma unroll
+      for (int i = 0; i < 128; i += 2) {
+        const float2 a = f2unpack(fma2(f2pack(__uint_as_float(x[i]), __uint_as_float(x[i + 1])), sl2, nm2));
+        float e0 = ex2_approx(a.x), e1 = ex2_approx(a.y);
+        if (!full) {
+          if (kv0 + i >= p.S) e0 = 0.0f;
+          if (kv0 + i + 1 >= p.S) e1 = 0.0f;
+        }
+        x[i] = __float_as_uint(e0);
+        x[i + 1] = __float_as_uint(e1);
+        s2[(i & 7) >> 1] = add2(s2[(i & 7) >> 1], f2pack(e0, e1));
+      }
+      float sum = 0.0f;
+      {
+        const float2 a = f2unpack(s2[0]), b = f2unpack(s2[1]), c = f2unpack(s2[2]), d = f2unpack(s2[3]);
+        sum = ((a.x + a.y) + (b.x + b.y)) + ((c.x + c.y) + (d.x + d.y));
+      }
+      l = l * alpha + sum;
+      if (j >= 1) {
+        // P_t V_{j-1} done: P_t's buffer is free and O_t holds the sum so far
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_full[t], (j - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      // 16-byte unit u of a 64-key chunk's 128-byte row holds keys [8u, 8u + 8)
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {
+        uint4 q;
+        q.x = pack2(__uint_as_float(x[g * 8 + 0]), __uint_as_float(x[g * 8 + 1]), (T*)nullptr);
+        q.y = pack2(__uint_as_float(x[g * 8 + 2]), __uint_as_float(x[g * 8 + 3]), (T*)nullptr);
+        q.z = pack2(__uint_as_float(x[g * 8 + 4]), __uint_as_float(x[g * 8 + 5]), (T*)nullptr);
+        q.w = pack2(__uint_as_float(x[g * 8 + 6]), __uint_as_float(x[g * 8 + 7]), (T*)nullptr);
+        const int u = g & 7;
+        *reinterpret_cast<uint4*>(prow + (g >> 3) * 16384 + ((u ^ (r & 7)) << 4)) = q;
+      }
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // the whole D-column row of O_t in one load round trip (the score
+        // registers are free again once P is stored)
+        const uint64_t a2 = f2pack(alpha, alpha);
+        uint32_t y[D];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c)
+          tmem_ld_32x32b_x32(t_lane + o_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&y[c * 32]));
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < D; i += 2) {
+          const float2 v = f2unpack(mul2(f2pack(__uint_as_float(y[i]), __uint_as_float(y[i + 1])), a2));
+          y[i] = __float_as_uint(v.x);
+          y[i + 1] = __float_as_uint(v.y);
+        }
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c)
+          tmem_st_32x32b_x32(t_lane + o_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&y[c * 32]));
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();   // P visible to the tensor core
+      mbar_arrive(&p_full[t]);
+      m_run = m_new;
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], (nkv - 1) & 1, abort_flag));
+    if (!ok) {
+      if (lane == 0) rec_err(p.err, abort_flag, kDevTimeoutAccFull);
+    } else {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const int row = q0 + t * 128 + r;
+      T* orow = reinterpret_cast<T*>(p.O) + (size_t(bh) * p.S + row) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t y[32];
+        tmem_ld_32x32b_x32(t_lane + o_col + c * 32, y);
+        tmem_ld_wait();
+        if (row < p.S) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 q;
+            q.x = pack2(__uint_as_float(y[g * 8 + 0]) * inv, __uint_as_float(y[g * 8 + 1]) * inv, (T*)nullptr);
+            q.y = pack2(__uint_as_float(y[g * 8 + 2]) * inv, __uint_as_float(y[g * 8 + 3]) * inv, (T*)nullptr);
+            q.z = pack2(__uint_as_float(y[g * 8 + 4]) * inv, __uint_as_float(y[g * 8 + 5]) * inv, (T*)nullptr);
+            q.w = pack2(__uint_as_float(y[g * 8 + 6]) * inv, __uint_as_float(y[g * 8 + 7]) * inv, (T*)nullptr);
+            reinterpret_cast<uint4*>(orow + c * 32)[g] = q;
+          }
+        }
       }
     }
   }
@@ -621,6 +976,48 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   return cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p);
 }
 
+template <int FMT, int D>
+cudaError_t launch_pp(const void* Q, const void* K, const void* V, void* O, int64_t BH, int64_t S, float scale,
+                      int* err, cudaStream_t s) {
+  using Cfg = PPCfg<D>;
+  auto kern = attention_pp_kernel<FMT, D>;
+  static_assert(Cfg::SMEM <= 232448, "shared memory budget");
+  static unsigned long long smem_set = 0;
+  cudaError_t e = set_smem_once(kern, int(Cfg::SMEM), smem_set);
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "cmpx attention (two-tile kernel) shared memory %zu: %s\n", size_t(Cfg::SMEM),
+                 cudaGetErrorString(e));
+    return e;
+  }
+  const int dt = FMT == 0 ? CMPX_F16 : CMPX_BF16;
+  CUtensorMap tq, tk, tv;
+  if (encode_tmap_3d(&tq, dt, Q, D, S, BH, D, S * D, 64, 128) != CMPX_OK ||
+      encode_tmap_3d(&tk, dt, K, D, S, BH, D, S * D, 64, 128) != CMPX_OK ||
+      encode_tmap_3d(&tv, dt, V, D, S, BH, D, S * D, 64, 128) != CMPX_OK)
+    return cudaErrorInvalidValue;
+  AttnParams p;
+  p.O = O;
+  p.S = int(S);
+  p.qtiles = int(((S + 127) / 128 + 1) / 2);   // CTAs (pairs of 128-row tiles) per (batch, head)
+  p.scale_log2 = scale * kLog2e;
+  p.err = err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(BH * p.qtiles));
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  apply_pdl(cfg, attr, 0);
+  e = cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p);
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa = {};
+    cudaFuncGetAttributes(&fa, kern);
+    std::fprintf(stderr, "cmpx attention (two-tile kernel) launch: %s (registers %d, max threads %d, smem %zu)\n",
+                 cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, size_t(Cfg::SMEM));
+  }
+  return e;
+}
+
 template <typename T>
 cudaError_t launch_simt_attn(const void* Q, const void* K, const void* V, void* O, int64_t BH, int64_t S, int64_t D,
                              float scale, cudaStream_t s) {
@@ -650,6 +1047,18 @@ int attention_threads_per_row() {
 // The softmax of the two-threads-per-row kernel in paired fp32 / three-input
 // max instructions (default), or in scalar ones with CMPX_ATTN_PACKED=0; the
 // results are the same bit for bit.
+// The tensor-core kernel: two query tiles per CTA (attention_pp_kernel) by
+// default; the one-tile kernel (attention_tc_kernel) with CMPX_ATTN_KERNEL=one
+// (measured on a B200, 8x8x1024x128 fp16: 588-589 vs 561-564 TFLOP/s).
+bool attention_pingpong() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("CMPX_ATTN_KERNEL");
+    v = (e != nullptr && e[0] == 'o') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 bool attention_packed() {
   static int v = -1;
   if (v < 0) {
@@ -694,7 +1103,14 @@ extern "C" int cmpx_attention(int dtype, const void* Q, const void* K, const voi
     if (BH * ((S + 127) / 128) > 0x7fffffffLL) return CMPX_ERR_UNSUPPORTED;
     const bool four = attention_threads_per_row() == 4;
     const bool packed = attention_packed();
-    if (dtype == CMPX_F16) {
+    if (attention_pingpong()) {
+      if (dtype == CMPX_F16)
+        e = D == 64 ? launch_pp<0, 64>(Q, K, V, O, BH, S, scale, err, stream)
+                    : launch_pp<0, 128>(Q, K, V, O, BH, S, scale, err, stream);
+      else
+        e = D == 64 ? launch_pp<1, 64>(Q, K, V, O, BH, S, scale, err, stream)
+                    : launch_pp<1, 128>(Q, K, V, O, BH, S, scale, err, stream);
+    } else if (dtype == CMPX_F16) {
       if (D == 64)
         e = four ? launch_tc<0, 64, 4, 0>(Q, K, V, O, BH, S, scale, err, stream)
              : packed ? launch_tc<0, 64, 2, 1>(Q, K, V, O, BH, S, scale, err, stream)

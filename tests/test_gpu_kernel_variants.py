@@ -59,18 +59,29 @@ torch.save(outs, sys.argv[1])
 
 
 def test_attention_packed_softmax_bit_identical(cuda, tmp_path):
-    """The tensor-core attention softmax in paired fp32 / three-input max
-    instructions (default) gives the same bits as its scalar form
+    """The one-tile tensor-core attention kernel's softmax in paired fp32 /
+    three-input max instructions (default) gives the same bits as its scalar form
     (CMPX_ATTN_PACKED=0): fp16 and bf16, D 64 and 128, ragged S, negative
     and large scales."""
     import torch
     res = {}
     for pk in ("1", "0"):
         f = tmp_path / f"attn{pk}.pt"
-        env = dict(os.environ, CMPX_ATTN_PACKED=pk, PYTHONPATH=os.path.dirname(HERE))
+        env = dict(os.environ, CMPX_ATTN_PACKED=pk, CMPX_ATTN_KERNEL="one", PYTHONPATH=os.path.dirname(HERE))
         r = subprocess.run([sys.executable, "-c", _ATTN_CHILD, str(f)], env=env, capture_output=True, text=True,
                            timeout=600)
         assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
         res[pk] = torch.load(f)
     for a, b in zip(res["1"], res["0"]):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+@pytest.mark.parametrize("kernel", ["pp", "one"])
+def test_attention_kernel_variant(cuda, kernel):
+    """The attention tests under each tensor-core attention kernel: two
+    128-row query tiles per CTA ("pp") and one tile per CTA ("one")."""
+    env = dict(os.environ, CMPX_ATTN_KERNEL=kernel)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.join(HERE, "test_gpu_attention.py")],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

@@ -71,7 +71,8 @@ def _ref_err(q, k, v, scale, want):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("D", [64, 128])
-@pytest.mark.parametrize("B,H,S", [(1, 1, 128), (2, 3, 200), (1, 2, 77), (1, 2, 1024), (2, 1, 389)],
+@pytest.mark.parametrize("B,H,S", [(1, 1, 128), (2, 3, 200), (1, 2, 77), (1, 2, 1024), (2, 1, 389), (1, 1, 1),
+                                   (2, 2, 300), (1, 1, 640)],
                          ids=lambda x: str(x))
 def test_tc_attention(cuda, dtype, D, B, H, S):
     q, k, v = _inputs(B, H, S, D, dtype, seed=S + D)

@@ -751,31 +751,31 @@ __global__ void __launch_bounds__(PPCfg<D>::THREADS, 1)
       const int kv0 = j * 128;
       const bool full = kv0 + 128 <= p.S;
       // the row maximum on the raw scores (of the negated ones for a negative
-      // scale), eight independent partial maxima
-      float mx8[8];
+      // scale), four independent partial maxima (eight, or eight partial sums
+      // below, and the compiler spills at the 168-register cap)
+      float mx4[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+      for (int i = 0; i < 4; ++i) mx4[i] = -INFINITY;
       if (full && sgn > 0.0f) {
 #pragma unroll
         for (int i = 0; i < 128; i += 2)
-          mx8[(i >> 1) & 7] = max3f(mx8[(i >> 1) & 7], __uint_as_float(x[i]), __uint_as_float(x[i + 1]));
+          mx4[(i >> 1) & 3] = max3f(mx4[(i >> 1) & 3], __uint_as_float(x[i]), __uint_as_float(x[i + 1]));
       } else if (full) {
 #pragma unroll
         for (int i = 0; i < 128; i += 2)
-          mx8[(i >> 1) & 7] = max3f(mx8[(i >> 1) & 7], -__uint_as_float(x[i]), -__uint_as_float(x[i + 1]));
+          mx4[(i >> 1) & 3] = max3f(mx4[(i >> 1) & 3], -__uint_as_float(x[i]), -__uint_as_float(x[i + 1]));
       } else {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
-          if (kv0 + i < p.S) mx8[i & 7] = fmaxf(mx8[i & 7], sgn * __uint_as_float(x[i]));
+          if (kv0 + i < p.S) mx4[i & 3] = fmaxf(mx4[i & 3], sgn * __uint_as_float(x[i]));
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float m_new = fmaxf(m_run, mx * sgn * sl);
       const float alpha = ex2_approx(m_run - m_new);   // 0 for the first block, 1 when m did not move
       // P = exp2(s * sl - m_new) in place of the scores, with the row sum
-      uint64_t s2[4];
+      uint64_t s2[2];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) s2[k] = f2pack(0.0f, 0.0f);
+      for (int k = 0; k < 2; ++k) s2[k] = f2pack(0.0f, 0.0f);
       const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-m_new, -m_new);
 #pragma unroll
       for (int i = 0; i < 128; i += 2) {
@@ -787,12 +787,12 @@ __global__ void __launch_bounds__(PPCfg<D>::THREADS, 1)
         }
         x[i] = __float_as_uint(e0);
         x[i + 1] = __float_as_uint(e1);
-        s2[(i & 7) >> 1] = add2(s2[(i & 7) >> 1], f2pack(e0, e1));
+        s2[(i >> 1) & 1] = add2(s2[(i >> 1) & 1], f2pack(e0, e1));
       }
       float sum = 0.0f;
       {
-        const float2 a = f2unpack(s2[0]), b = f2unpack(s2[1]), c = f2unpack(s2[2]), d = f2unpack(s2[3]);
-        sum = ((a.x + a.y) + (b.x + b.y)) + ((c.x + c.y) + (d.x + d.y));
+        const float2 a = f2unpack(s2[0]), b = f2unpack(s2[1]);
+        sum = (a.x + a.y) + (b.x + b.y);
       }
       l = l * alpha + sum;
       if (j >= 1) {
@@ -1049,7 +1049,7 @@ int attention_threads_per_row() {
 // results are the same bit for bit.
 // The tensor-core kernel: two query tiles per CTA (attention_pp_kernel) by
 // default; the one-tile kernel (attention_tc_kernel) with CMPX_ATTN_KERNEL=one
-// (measured on a B200, 8x8x1024x128 fp16: 588-589 vs 561-564 TFLOP/s).
+// (measured on a B200, 8x8x1024x128 fp16: 605-608 vs 553-568 TFLOP/s).
 bool attention_pingpong() {
   static int v = -1;
   if (v < 0) {

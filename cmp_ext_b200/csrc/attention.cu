@@ -532,11 +532,13 @@ __global__ void __launch_bounds__(AttnCfg<D, TPR>::THREADS, 1)
 // attention_pp_kernel: one CTA owns 256 query rows (tiles A and B) of one
 // (batch, head), so the tensor core works on one tile's products while the
 // other tile is in softmax:
-//   * warp 0 (TMA): both Q tiles once, then K_0, V_0, K_1, V_1, ... through
-//     one shared ring of NS slots;
+//   * warp 0 (TMA): both Q tiles once, then K_0, V_0, K_1, V_1, ... into
+//     a K ring and a V ring;
 //   * warp 1 (one thread): S_t = Q_t K_j^T into tile t's 128-column TMEM
-//     buffer as soon as tile t's softmax has read the previous S_t out, and
-//     O_t += P_t V_j into tile t's D-column accumulator once P_t is written;
+//     buffer as soon as tile t's softmax has read the previous S_t out and
+//     K_j is in, and O_t += P_t V_j into tile t's D-column accumulator once
+//     P_t is written and V_j is in, for both tiles in whichever order their
+//     inputs become ready;
 //   * warps 2-5 (tile A) and 6-9 (tile B): one thread per query row, holding
 //     the row's 128 scores of a block in registers: the running maximum and
 //     sum in fp32, P = exp2(s * scale * log2 e - m) as 16-bit values into
@@ -551,7 +553,12 @@ struct PPCfg {
   static constexpr int QCH = D / 64;
   static constexpr int TILE_BYTES = 128 * D * 2;
   static constexpr int P_BYTES = 128 * 128 * 2;
-  static constexpr int NS = D == 128 ? 3 : 6;      // K/V ring slots
+  // K_j in slot j % KS, V_j in slot KS + j % VS.  With one K slot, K_{j+1}
+  // loads as soon as the last Q K_j^T is done; two V slots let V_{j+1} load a
+  // whole block ahead of its first P V.
+  static constexpr int KS = D == 128 ? 1 : 3;
+  static constexpr int VS = D == 128 ? 2 : 3;
+  static constexpr int NS = KS + VS;               // K/V slots
   static constexpr size_t SMEM = size_t(TILE_BYTES) * (2 + NS) + 2 * P_BYTES + 1024 + 256;
   static constexpr uint32_t TMEM_COLS = 512;       // S_A S_B (128 each), O_A O_B (D each)
   static_assert(D == 64 || D == 128, "tensor-core attention supports D = 64 or 128");
@@ -626,29 +633,35 @@ __global__ void __launch_bounds__(PPCfg<D>::THREADS, 1)
 #pragma unroll
         for (int c = 0; c < Cfg::QCH; ++c)
           tma_load_3d(sQ + t * Cfg::TILE_BYTES + c * 16384, &tmQ, q_full, c * 64, q0 + t * 128, bh);
-      // items 2j (K_j) and 2j + 1 (V_j) through the ring
-      int issued = 0;
+      // K_0, V_0, K_1, V_1, ... each into its own ring
+      int issued[NS];
+#pragma unroll
+      for (int i = 0; i < NS; ++i) issued[i] = 0;
       bool ok = true;
-      for (int i = 0; i < 2 * nkv; ++i) {
-        const int slot = i % NS;
-        if (!mbar_wait(&kv_empty[slot], ((i / NS) & 1) ^ 1, abort_flag)) {
+      for (int i = 0; i < 2 * nkv && ok; ++i) {
+        const int j = i >> 1;
+        const bool isv = (i & 1) != 0;
+        const int slot = isv ? Cfg::KS + j % Cfg::VS : j % Cfg::KS;
+        const int use = isv ? j / Cfg::VS : j / Cfg::KS;   // earlier loads into this slot
+        if (!mbar_wait(&kv_empty[slot], (use & 1) ^ 1, abort_flag)) {
           rec_err(p.err, abort_flag, kDevTimeoutEmpty);
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&kv_full[slot], Cfg::TILE_BYTES);
-        const CUtensorMap* m = (i & 1) ? &tmV : &tmK;
+        const CUtensorMap* m = isv ? &tmV : &tmK;
 #pragma unroll
         for (int c = 0; c < Cfg::QCH; ++c)
-          tma_load_3d(sKV + slot * Cfg::TILE_BYTES + c * 16384, m, &kv_full[slot], c * 64, (i >> 1) * 128, bh);
-        ++issued;
+          tma_load_3d(sKV + slot * Cfg::TILE_BYTES + c * 16384, m, &kv_full[slot], c * 64, j * 128, bh);
+        issued[slot] = use + 1;
       }
       if (!ok) {
-        // let the copies in flight land before the CTA exits (bounded waits)
+        // let the copies in flight land before the CTA exits (bounded waits;
+        // a slot's loads complete in order, so its last one is enough)
         volatile int never = 0;
         mbar_wait(q_full, 0, &never);
-        for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
-          mbar_wait(&kv_full[i % NS], (i / NS) & 1, &never);
+        for (int i = 0; i < NS; ++i)
+          if (issued[i] > 0) mbar_wait(&kv_full[i], (issued[i] - 1) & 1, &never);
       }
     }
   } else if (warp == 1) {
@@ -656,20 +669,12 @@ __global__ void __launch_bounds__(PPCfg<D>::THREADS, 1)
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, abort_flag);
       if (!ok) rec_err(p.err, abort_flag, kDevTimeoutFull);
-      auto kv_wait = [&](int i) -> bool {
-        if (mbar_wait(&kv_full[i % NS], (i / NS) & 1, abort_flag)) return true;
-        rec_err(p.err, abort_flag, kDevTimeoutFull);
-        return false;
-      };
-      auto wait_or_fail = [&](uint64_t* bar, int parity, int code) -> bool {
-        if (mbar_wait(bar, uint32_t(parity), abort_flag)) return true;
-        rec_err(p.err, abort_flag, code);
-        return false;
-      };
+      auto k_ready = [&](int j) { return mbar_try_wait(&kv_full[j % Cfg::KS], (j / Cfg::KS) & 1); };
+      auto v_ready = [&](int j) { return mbar_try_wait(&kv_full[Cfg::KS + j % Cfg::VS], (j / Cfg::VS) & 1); };
       auto qk = [&](int t, int j) {
         tc_fence_after();
         const uint32_t q_addr = smem_u32(sQ + t * Cfg::TILE_BYTES);
-        const uint32_t k_addr = smem_u32(sKV + ((2 * j) % NS) * Cfg::TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sKV + (j % Cfg::KS) * Cfg::TILE_BYTES);
         const uint32_t d_tmem = tmem_base + uint32_t(t * 128);
 #pragma unroll
         for (int c = 0; c < Cfg::QCH; ++c)
@@ -682,7 +687,7 @@ __global__ void __launch_bounds__(PPCfg<D>::THREADS, 1)
       auto pv = [&](int t, int j) {
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sP + t * Cfg::P_BYTES);
-        const uint32_t v_addr = smem_u32(sKV + ((2 * j + 1) % NS) * Cfg::TILE_BYTES);
+        const uint32_t v_addr = smem_u32(sKV + (Cfg::KS + j % Cfg::VS) * Cfg::TILE_BYTES);
         const uint32_t d_tmem = tmem_base + 256u + uint32_t(t * D);
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2)
@@ -693,28 +698,44 @@ __global__ void __launch_bounds__(PPCfg<D>::THREADS, 1)
                     (j | c2 | kk) != 0 ? 1u : 0u);
         mma_commit(&o_full[t]);
       };
-      if (ok) ok = kv_wait(0);
+      if (ok) {
+        ok = mbar_wait(&kv_full[0], 0, abort_flag);
+        if (!ok) rec_err(p.err, abort_flag, kDevTimeoutFull);
+      }
       if (ok) {
         for (int t = 0; t < nt; ++t) qk(t, 0);
         mma_commit(&kv_empty[0]);
       }
+      // Per block j, for both tiles t: S_t = Q_t K_{j+1}^T (needs K_{j+1}
+      // and S_t read out) and O_t += P_t V_j (needs P_t and V_j), each issued
+      // as soon as its inputs are ready (bounded polling), so a late tile
+      // does not hold up the other.
       for (int j = 0; ok && j < nkv; ++j) {
         const bool more = j + 1 < nkv;
-        if (more) ok = kv_wait(2 * j + 2);
-        for (int t = 0; ok && t < nt; ++t) {
-          if (more) {
-            ok = wait_or_fail(&s_free[t], j & 1, kDevTimeoutAccEmpty);
-            if (!ok) break;
-            qk(t, j + 1);
+        bool need_qk[2] = {more, more && nt > 1};
+        bool need_pv[2] = {true, nt > 1};
+        bool k_in = false, v_in = false;
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t it = 1; need_qk[0] || need_qk[1] || need_pv[0] || need_pv[1]; ++it) {
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (need_qk[t] && (k_in || (k_in = k_ready(j + 1))) && mbar_try_wait(&s_free[t], j & 1)) {
+              qk(t, j + 1);
+              need_qk[t] = false;
+              if (!need_qk[0] && !need_qk[1]) mma_commit(&kv_empty[(j + 1) % Cfg::KS]);
+            }
+            if (need_pv[t] && (v_in || (v_in = v_ready(j))) && mbar_try_wait(&p_full[t], j & 1)) {
+              pv(t, j);
+              need_pv[t] = false;
+            }
           }
-          ok = wait_or_fail(&p_full[t], j & 1, kDevTimeoutFull);
-          if (ok && t == 0) ok = kv_wait(2 * j + 1);
-          if (ok) pv(t, j);
+          if ((it & 63u) == 0 && (*abort_flag || globaltimer_ns() - t0 > CMPX_WAIT_TIMEOUT_NS)) {
+            rec_err(p.err, abort_flag, kDevTimeoutFull);
+            ok = false;
+            break;
+          }
         }
-        if (ok) {
-          if (more) mma_commit(&kv_empty[(2 * j + 2) % NS]);
-          mma_commit(&kv_empty[(2 * j + 1) % NS]);
-        }
+        if (ok) mma_commit(&kv_empty[Cfg::KS + j % Cfg::VS]);
       }
       if (!ok) {
         mma_commit(drain);
@@ -1049,7 +1070,7 @@ int attention_threads_per_row() {
 // results are the same bit for bit.
 // The tensor-core kernel: two query tiles per CTA (attention_pp_kernel) by
 // default; the one-tile kernel (attention_tc_kernel) with CMPX_ATTN_KERNEL=one
-// (measured on a B200, 8x8x1024x128 fp16: 605-608 vs 553-568 TFLOP/s).
+// (measured on a B200, 8x8x1024x128 fp16: 624-626 vs 544-546 TFLOP/s).
 bool attention_pingpong() {
   static int v = -1;
   if (v < 0) {
